@@ -1,0 +1,141 @@
+"""The NumPy oracle against fixtures produced by the reference's own code (CPU only)."""
+
+import numpy as np
+import pytest
+
+import inputs
+from oracle import attention, polar, runtime, vquant
+
+
+def _fmt(overrides):
+    return dict(l1_bits=overrides.get("k_angle_bits_level1", 4), deep_bits=overrides.get("k_angle_bits_deep", 4),
+                split_dim=overrides.get("split_dim", 64))
+
+
+@pytest.mark.parametrize("name", list(inputs.CODEC_CASES))
+def test_codec_bit_exact(name, golden):
+    overrides, _, _ = inputs.CODEC_CASES[name]
+    fmt = _fmt(overrides)
+    k, v = inputs.codec_inputs(name)
+    enc = polar.encode_block(k, int8_radii=overrides.get("use_int8_radii", False), **fmt)
+    g = lambda f: golden[f"codec/{name}/{f}"]
+    np.testing.assert_array_equal(enc["radii"], g("radii"))
+    assert enc["radii"].dtype == g("radii").dtype
+    np.testing.assert_array_equal(enc["angle_codes_l1"], g("angle_codes_l1"))
+    np.testing.assert_array_equal(enc["angle_codes_deep"], g("angle_codes_deep"))
+    if overrides.get("use_int8_radii"):
+        np.testing.assert_array_equal(enc["radii_scales"], g("radii_scales"))
+    codes, scales = vquant.quantize(v)
+    np.testing.assert_array_equal(codes, g("v_codes").reshape(codes.shape))
+    np.testing.assert_array_equal(scales, g("v_scales").reshape(scales.shape))
+    # Decoder: same float16 keys, bit for bit.
+    dec = polar.decode_block(enc["radii"], enc["angle_codes_l1"], enc["angle_codes_deep"], enc["radii_scales"], **fmt)
+    np.testing.assert_array_equal(dec.view(np.uint16), g("k_decoded").reshape(dec.shape).view(np.uint16))
+    if name == "default_f16":
+        np.testing.assert_array_equal(vquant.dequantize(codes, scales), g("v_dequant").reshape(codes.shape))
+
+
+def test_packed_lengths_contract():
+    # tests/benchmarks/test_turbo_polar_offline.py:26-34
+    k, _ = inputs.codec_inputs("default_f16")
+    enc = polar.encode_block(k)
+    assert enc["radii"].shape == (1, 4, 64, 64)
+    assert enc["angle_codes_l1"].shape == (1, 4, 64, (32 + 1) // 2)
+    assert enc["angle_codes_deep"].shape == (1, 4, 64, polar.packed_len(32, 4))
+    enc2 = polar.encode_block(k, l1_bits=8, deep_bits=2, split_dim=32)
+    assert enc2["angle_codes_l1"].shape == (1, 4, 64, 16)
+    assert enc2["angle_codes_deep"].shape == (1, 4, 64, 12)
+
+
+def test_c1_runtime_and_fallback_attention(golden, golden_meta):
+    ks, vs, q = inputs.c1_inputs()
+    model = runtime.CacheModel(4)
+    for i in range(ks.shape[0]):
+        model.append(ks[i], vs[i])
+    assert model.telemetry() == pytest.approx(golden_meta["c1"]["telemetry"])
+    pages = model.pages()
+    for f in ("radii", "angle_codes_l1", "angle_codes_deep", "v_codes", "v_scales"):
+        np.testing.assert_array_equal(pages[f], golden[f"c1/{f}"][0])
+    np.testing.assert_array_equal(model.partial_k, golden["c1/tail_k"])
+    fmt = model.fmt
+    out = attention.attention_dense_tail(q[0], pages, fmt, model.partial_k[0], model.partial_v[0], 100, 1 / np.sqrt(128))
+    ref = golden["c1/out"][0].astype(np.float64)
+    # The reference fallback reduces in float16; the oracle in float64.
+    assert np.max(np.abs(out - ref)) < 2e-3
+    k_dec, _ = attention.decode_pages(pages, fmt)
+    sc = attention.fused_scores(q[0], k_dec, 1 / np.sqrt(128))
+    assert np.max(np.abs(sc - golden["c1/scores"][0].astype(np.float64))) < 1e-2
+
+
+@pytest.mark.parametrize("t", inputs.SHAPE_TS)
+@pytest.mark.parametrize("gqa", (1, 4))
+def test_shape_matrix_telemetry_and_partial_encode(t, gqa, golden, golden_meta):
+    tag = f"shape/T{t}_g{gqa}"
+    k, v = inputs.shape_inputs(t, gqa)
+    model = runtime.CacheModel(4 // gqa, split_dim=0)
+    model.append(k, v)
+    assert model.telemetry() == pytest.approx(golden_meta[tag]["telemetry"])
+    assert model.telemetry()["partial_tokens"] == t % 64
+    assert model.telemetry()["total_blocks"] == t // 64
+    if gqa == 4:
+        blocks = list(model.blocks)
+        part = model.padded_partial()
+        if part is not None:
+            blocks.append(part)
+        for f in ("radii", "angle_codes_l1", "angle_codes_deep", "v_codes"):
+            got = np.stack([b[f][0] for b in blocks], axis=1)
+            np.testing.assert_array_equal(got, golden[f"{tag}/{f}"][0])
+
+
+def test_growth_telemetry(golden_meta):
+    model = runtime.CacheModel(2)
+    for (k, v), want in zip(inputs.growth_inputs(), golden_meta["growth"]["telemetry"]):
+        model.append(k, v)
+        assert model.telemetry() == pytest.approx(want)
+
+
+def test_telemetry_known_answer_c1(golden_meta):
+    # Known answer: 100 tokens, 4 KV heads, default format (296 B/token/head for pages).
+    t = golden_meta["c1"]["telemetry"]
+    assert t["dense_kv_bytes"] == 1 * 4 * 100 * 128 * 2 * 2 == 204800
+    assert t["actual_cache_bytes"] == 64 * 4 * 296 + 36 * 4 * 128 * 2 * 2 == 149504
+    assert t["total_blocks"] == 1 and t["partial_tokens"] == 36
+
+
+def test_codec_known_answers():
+    # Hand-derived from encoder.py:46-55 with float16 constants pi=3.140625, 2pi=6.28125.
+    k = np.zeros((1, 1, 1, 128), np.float16)
+    k[..., 0:2] = (1, 0)    # theta=0 -> norm=0.5 -> 7.5 -> round-half-even 8
+    k[..., 2:4] = (-1, 0)   # theta=pi(fp16) -> shifted=6.28125 -> norm=1 -> 15
+    k[..., 4:6] = (0, 1)    # theta=pi/2 -> 1.5703125; +pi=4.7109375; /2pi=0.75 -> 11.25 -> 11
+    k[..., 6:8] = (0, -1)   # theta=-pi/2 -> 1.5703125 -> norm 0.25 -> 3.75 -> 4
+    enc = polar.encode_block(k)
+    codes = polar.unpack_4bit(enc["angle_codes_l1"], 32)[0, 0, 0]
+    assert list(codes[:4]) == [8, 15, 11, 4]
+    assert list(enc["radii"][0, 0, 0, :4]) == [1, 1, 1, 1]
+    # Zero pair: atan2(0, 0) = 0 -> code 8 with radius 0.
+    assert codes[4] == 8 and enc["radii"][0, 0, 0, 4] == 0
+    # V: group max 127 -> scale exactly 1, codes equal the inputs.
+    v = np.zeros((1, 128), np.float16)
+    v[0, :32] = np.arange(-15, 17)
+    v[0, 31] = 127
+    c, s = vquant.quantize(v)
+    assert s[0, 0] == 1 and list(c[0, :31]) == list(range(-15, 16)) and c[0, 31] == 127
+    assert s[0, 1] == np.float16(1e-4) and not c[0, 32:].any()
+
+
+def test_adapter_sequence_oracle(golden):
+    """Oracle attention over the cache contents after every decode step agrees with the
+    reference adapter's outputs (dense-only, compressed+tail and block-boundary branches)."""
+    qs, ks, vs = inputs.adapter_inputs()
+    for name, overrides in inputs.ADAPTER_CASES.items():
+        fmt = _fmt(overrides)
+        model = runtime.CacheModel(2, int8_radii=True, **fmt)
+        want = golden[f"adapter/{name}/out"]
+        for i in range(qs.shape[0]):
+            model.append(ks[i], vs[i])
+            pages = model.pages()
+            tk = model.partial_k[0] if model.partial_k is not None else None
+            tv = model.partial_v[0] if model.partial_v is not None else None
+            out = attention.attention_dense_tail(qs[i][0, :, 0, :], pages, fmt, tk, tv, i + 1, 1 / np.sqrt(128))
+            assert np.max(np.abs(out - want[i][0].astype(np.float64))) < 3e-3, (name, i)
