@@ -1,0 +1,176 @@
+/*
+ * turbopolar.h -- C ABI of libturbopolar.so, the B200 (sm_100a) implementation of
+ * TurboPolar's compressed-KV single-batch decode path.
+ *
+ * The reference (dawsonblock/Turbopolar) runs this path through MLX on Apple GPUs.  Each
+ * entry point below replaces one reference interface, cited as path:line inside that
+ * project.  Conventions shared by every entry point:
+ *
+ *   - Plain pointers and sizes only.  Device pointers are CUDA global-memory addresses on
+ *     the current device; `stream` is a cudaStream_t passed as void*.
+ *   - Nothing allocates: every buffer (page pools, tail, state words, workspace, outputs)
+ *     belongs to the caller.  Every launch is asynchronous on `stream`.
+ *   - The return value is a tp_status; on failure tp_last_error() returns a message for
+ *     the calling thread.  TP_ERR_INVALID maps to Python ValueError, TP_ERR_UNSUPPORTED to
+ *     NotImplementedError, TP_ERR_CUDA to RuntimeError.
+ *   - Batch size 1, head_dim 128, block (page) size 64 tokens, grouped int8 values with 32
+ *     channels per group: the reference's supported contract
+ *     (rfsn_v11/candidates/turbo_polar_config.py:27-55).
+ */
+#ifndef TURBOPOLAR_H_
+#define TURBOPOLAR_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TP_HEAD_DIM 128
+#define TP_PAGE_TOKENS 64
+#define TP_V_GROUP 32
+/* Floats per partial record: m (log2 domain), l, then 128 unnormalised outputs. */
+#define TP_PARTIAL_FLOATS 130
+
+typedef enum tp_status {
+  TP_OK = 0,
+  TP_ERR_INVALID = 1,     /* bad argument or state (ValueError) */
+  TP_ERR_UNSUPPORTED = 2, /* outside the supported contract (NotImplementedError) */
+  TP_ERR_CUDA = 3         /* launch / runtime failure (RuntimeError) */
+} tp_status;
+
+typedef enum tp_dtype { TP_F16 = 0, TP_F32 = 1 } tp_dtype;
+
+/* Key format: the fields of TurboPolarConfig that shape a PolarKeyBlock
+ * (rfsn_v11/candidates/turbo_polar_config.py:11-21, rfsn_v11/quant/polar/encoder.py:24-98). */
+typedef struct tp_format {
+  int32_t l1_bits;    /* k_angle_bits_level1: 4 or 8 */
+  int32_t deep_bits;  /* k_angle_bits_deep: 2, 4 or 8 */
+  int32_t split_dim;  /* even, 0..128: pairs [0, split_dim/2) use level-1 codes */
+  int32_t int8_radii; /* 0: float16 radii; 1: log-int8 radii + one float16 scale per page */
+} tp_format;
+
+/* Device page pool: one structure-of-arrays store per field, pages of one KV head
+ * contiguous, in the reference's block-storage shapes without the batch axis
+ * (rfsn_v11/generation/storage.py:17-169, views at :89-102 and :160-169):
+ *   radii            [H_kv][page_capacity][64][64]  float16 (int8 when fmt.int8_radii)
+ *   radii_scales     [H_kv][page_capacity]          float16 (fmt.int8_radii only, else NULL)
+ *   angle_codes_l1   [H_kv][page_capacity][64][l1_row_bytes]   uint8, packed
+ *   angle_codes_deep [H_kv][page_capacity][64][deep_row_bytes] uint8, packed
+ *   v_codes          [H_kv][page_capacity][64][128] int8
+ *   v_scales         [H_kv][page_capacity][64][4]   float16
+ * Row byte counts come from tp_row_bytes().  Base pointers must be 16-byte aligned. */
+typedef struct tp_page_pool {
+  void* radii;
+  void* radii_scales;
+  void* angle_codes_l1;
+  void* angle_codes_deep;
+  void* v_codes;
+  void* v_scales;
+  int32_t num_kv_heads;
+  int32_t page_capacity;
+  tp_format fmt;
+} tp_page_pool;
+
+/* Dense tail (the reference's partial block, rfsn_v11/generation/turbo_polar_cache.py:110-126):
+ * k and v are [H_kv][64][128] in `dtype`, the first tail_len token rows valid. */
+typedef struct tp_tail {
+  void* k;
+  void* v;
+  int32_t dtype; /* tp_dtype */
+} tp_tail;
+
+/* Cache state.  Kernels that take `const int32_t* d_state` read these four words from
+ * device memory when the pointer is non-NULL (CUDA-graph replay) and from the struct
+ * passed by value otherwise.  Word order: n_pages, tail_len, seq_len, first_page, then
+ * an error word written by tp_append and a ticket word it uses internally (both zero at
+ * rest).  first_page is the absolute index of local page 0 (non-zero on sequence shards);
+ * token l of local page p sits at absolute position (first_page + p) * 64 + l, tail token
+ * t at (first_page + n_pages) * 64 + t, and positions >= seq_len are masked
+ * (rfsn_v11/kernels/turbo_polar/metal.py:317-319). */
+typedef struct tp_state {
+  int32_t n_pages;
+  int32_t tail_len;
+  int32_t seq_len;
+  int32_t first_page;
+} tp_state;
+#define TP_STATE_WORDS 6
+
+/* Bytes per token row of the level-1 and deep code arrays for `fmt`
+ * (tests/benchmarks/test_turbo_polar_offline.py:26-34).  Returns TP_ERR_UNSUPPORTED for a
+ * format outside turbo_polar_config.py / encoder.py's accepted bit widths. */
+int tp_row_bytes(const tp_format* fmt, int32_t* l1_row_bytes, int32_t* deep_row_bytes);
+
+/* Encode n_pages full 64-token blocks of dense keys/values into pool pages
+ * [dst_page, dst_page + n_pages) of every KV head.  Token t of head h of the source is at
+ * k + (h * head_stride + (src_token0 + t) * token_stride) elements (innermost 128 contiguous),
+ * same for v.  Bit-exact with PolarQuantEncoder.encode_block + GroupedVQuantizer.quantize_block
+ * (rfsn_v11/quant/polar/encoder.py:24-130, rfsn_v11/quant/v_quant/encoder.py:16-30) as called
+ * by TurboPolarKVCacheRuntime._flush_block (rfsn_v11/generation/turbo_polar_cache.py:128-161).
+ * If d_state is non-NULL, n_pages is added to its n_pages word and 64*n_pages to seq_len after
+ * the encode (used when a long append encodes whole pages straight from its input). */
+int tp_encode_pages(const tp_page_pool* pool, const void* k, const void* v, int32_t dtype,
+                    int64_t head_stride, int64_t token_stride, int64_t src_token0,
+                    int32_t n_pages, int32_t dst_page, int32_t* d_state, void* stream);
+
+/* Append n_tokens (1..64) tokens to the dense tail at the device-side tail_len; when the
+ * tail reaches 64 tokens, encode it into page n_pages and empty it; then advance the state
+ * words (TurboPolarKVCacheRuntime.append, rfsn_v11/generation/turbo_polar_cache.py:106-126).
+ * The caller keeps tail_len + n_tokens <= 64.  A violated bound or a full pool sets the
+ * state's error word (1: tail overflow, 2: page pool full) and changes nothing else. */
+int tp_append(const tp_page_pool* pool, const tp_tail* tail, int32_t* d_state, const void* k_new,
+              const void* v_new, int32_t dtype, int64_t head_stride, int64_t token_stride,
+              int32_t n_tokens, void* stream);
+
+/* Workspace bytes tp_decode_attention needs for this head layout.  The workspace must be
+ * zero-filled once when allocated; every launch leaves its counters at zero again. */
+size_t tp_decode_attention_workspace_size(int32_t num_kv_heads, int32_t num_q_heads);
+
+/* Fused decode attention over compressed pages plus the dense tail, for one query token:
+ *   out[hq][:] = softmax_t(scale * q[hq] . K[hq / G][t]) @ V[hq / G]     (fp16, [H_q][128])
+ * Replaces MetalKernelBridge.execute_online_attention_quant_v_dense_tail and
+ * execute_online_attention_quant_v (rfsn_v11/kernels/turbo_polar/metal.py:651-792, kernels
+ * tqpolar_online_attention.metal:197-629) with the reference's CPU fallback as the numeric
+ * target (metal.py:267-332).  q is [H_q][128] in q_dtype (float32 queries are rounded to
+ * float16 as the reference's kernels read them).  With partial_out non-NULL the kernel
+ * writes, instead of `out`, one unnormalised partial per query head
+ * [H_q][TP_PARTIAL_FLOATS] = (m in log2 units, l, o[128]) for a cross-shard log-sum-exp
+ * merge (tp_combine_partials).  `state` is used when d_state is NULL. */
+int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state state,
+                        const int32_t* d_state, const void* q, int32_t q_dtype,
+                        int32_t num_q_heads, float scale, void* out, float* partial_out,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Merge n_parts partial records per query head, laid out [n_parts][H_q][TP_PARTIAL_FLOATS]
+ * (the all-gathered output of tp_decode_attention on each sequence shard), into fp16
+ * out[H_q][128]: M = max m_r, L = sum l_r 2^(m_r - M), O = sum o_r 2^(m_r - M) / L. */
+int tp_combine_partials(const float* partials, int32_t n_parts, int32_t num_q_heads, void* out,
+                        void* stream);
+
+/* Scores only: scores[hq][p*64 + l] = scale * q[hq] . K[hq / G][page p][l] for local pages
+ * [0, n_pages), fp16 [H_q][n_pages*64].  Replaces MetalKernelBridge.execute_fused_qk
+ * (rfsn_v11/kernels/turbo_polar/metal.py:494-530, tqpolar_fused_qk.metal:4-100); accumulates
+ * in float32 where the Metal kernel used float16. */
+int tp_fused_scores(const tp_page_pool* pool, int32_t n_pages, const void* q, int32_t q_dtype,
+                    int32_t num_q_heads, float scale, void* scores, void* stream);
+
+/* Decompress pages [first_page, first_page + n_pages) to dense fp16 keys and values,
+ * k_out/v_out [H_kv][n_pages*64][128] (PolarQuantDecoder.decode_block and
+ * GroupedVQuantizer.dequantize_block, rfsn_v11/quant/polar/decoder.py:7-67,
+ * rfsn_v11/quant/v_quant/encoder.py:32-38; the prefill decompress-on-read path of
+ * benchmarks/turbopolar_fast_attention.py:56-86). */
+int tp_decode_pages(const tp_page_pool* pool, int32_t first_page, int32_t n_pages, void* k_out,
+                    void* v_out, void* stream);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* tp_last_error(void);
+
+/* ABI version of this library. */
+int tp_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TURBOPOLAR_H_ */

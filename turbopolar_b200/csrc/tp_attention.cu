@@ -1,0 +1,764 @@
+// Fused decode attention over compressed KV pages + dense tail (sm_100a).
+//
+// Replaces the reference's Metal kernels tqpolar_online_attention_quant_v[_dense_tail]
+// (rfsn_v11/kernels/turbo_polar/tqpolar_online_attention.metal:197-629) with the numerics of
+// the bridge's CPU fallback (rfsn_v11/kernels/turbo_polar/metal.py:293-332) as the target.
+//
+// Work decomposition.  A "unit" is one 64-token page of one (KV head, query chunk), or that
+// head's dense tail.  The units of all heads form one flat list that is cut into gridDim.x
+// contiguous ranges, one per CTA, so every SM streams the same number of pages whatever the
+// head count or context length; a range spans at most two heads ("segments").  Inside a CTA
+// each of the 4 warps takes a contiguous quarter of each segment and streams its pages through
+// a private double buffer in shared memory (cp.async, 16 bytes per lane, rows of radii and
+// value codes XOR-swizzled so the fragment loads below are bank-conflict free).
+//
+// Per page a warp computes, with mma.sync m16n8k16 (fp16 in, fp32 accumulate):
+//   S^T[token][head] = K[token][dim] . Q^T[dim][head]      M = 16 tokens, N = 8 query heads
+// where every lane decodes exactly the key pairs its A fragment holds: lane (g, t) owns pairs
+// [16t, 16t+16) of tokens g and g+8, each pair k = radius * (cos, sin)(code) from a 16-entry
+// half2 table, so no decoded key ever touches shared memory.  Online softmax runs in the
+// base-2 domain on the accumulator fragments; P is converted to fp16 and transposed into the
+// B operand with movmatrix, the per-(token, 32-channel group) value scales are folded into
+// P (one copy of B per group), and
+//   O^T[dim][head] += V'^T[dim][token] . (P * scale_g)^T[token][head]
+// runs with V' = code + 1152 produced by a byte permute into the fp16 exponent (0x64xx = 1024
+// + byte, byte = code ^ 0x80).  The bias is removed at the end with a ones-row tile per group
+// that accumulates sum_t P*scale_g alongside (O = O' - 1152 * sum).
+//
+// Split combine.  Warps of a CTA merge through shared memory; CTAs that share a head write a
+// partial (m, l, o[128]) to the workspace and the last to arrive (atomic ticket per head)
+// merges them and writes the fp16 output, then resets the ticket, all in the same launch.
+#include <cfloat>
+
+#include "tp_common.cuh"
+
+namespace tp {
+
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxHeads = 8;  // query heads per unit (N of the mma)
+constexpr int kPartialStride = kMaxHeads * TP_PARTIAL_FLOATS;  // floats per workspace slot
+constexpr int kLutEntries = 256;
+
+struct AttnParams {
+  const uint8_t* radii;
+  const __half* radii_scales;
+  const uint8_t* l1;
+  const uint8_t* deep;
+  const int8_t* v_codes;
+  const __half* v_scales;
+  int page_capacity;
+  int l1_bits, deep_bits, l1_pairs, l1_row, deep_row, radii_row, int8_radii;
+  int radii_page, l1_page, deep_page;  // bytes per page per head
+  const void* tail_k;
+  const void* tail_v;
+  int tail_f32;
+  tp_state st;
+  const int32_t* d_state;
+  const void* q;
+  int q_f32;
+  int num_q_heads, num_kv_heads, group, nqc;
+  float scale_log2;
+  __half* out;
+  float* partial_out;
+  float* ws_partials;
+  int* ws_counters;
+  int stage_bytes, off_vcodes, off_l1, off_deep, off_vscales;
+  int smem_merge_off, smem_stage_off;
+};
+
+__device__ __forceinline__ int64_t clamp64(int64_t x, int64_t lo, int64_t hi) { return x < lo ? lo : (x > hi ? hi : x); }
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+  return h2_as_u32(__hmul2(u32_as_h2(a), u32_as_h2(b)));
+}
+__device__ __forceinline__ uint32_t bcast_lo(uint32_t w) { return prmt(w, 0, 0x1010); }
+__device__ __forceinline__ uint32_t bcast_hi(uint32_t w) { return prmt(w, 0, 0x3232); }
+
+// Byte offset of 16-byte chunk `c` of row `r` in a swizzled 128-byte-row tile.
+__device__ __forceinline__ int swz128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+// ----------------------------------------------------------------------------- per-warp state
+struct WarpAcc {
+  float o[8][4];     // O'^T tiles: tile md rows d = 32(md/2) + 4g + 2(md%2) (+1), cols heads 2t, 2t+1
+  float ones[4][4];  // per value group: sum_t P*scale (every row identical)
+  float m[2], l[2];  // running max (log2 units) and lane-partial sum for heads 2t, 2t+1
+};
+
+__device__ __forceinline__ void acc_reset(WarpAcc& A) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) A.o[i][j] = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) A.ones[i][j] = 0.f;
+  A.m[0] = A.m[1] = -INFINITY;
+  A.l[0] = A.l[1] = 0.f;
+}
+
+// Online-softmax update from the raw score fragments of one 64-token unit; returns P in sc.
+__device__ __forceinline__ void softmax_update(WarpAcc& A, float (&sc)[4][4], float c) {
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) {
+    mx0 = fmaxf(mx0, fmaxf(sc[mt][0], sc[mt][2]));
+    mx1 = fmaxf(mx1, fmaxf(sc[mt][1], sc[mt][3]));
+  }
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+  }
+  const float mn0 = fmaxf(A.m[0], mx0 * c), mn1 = fmaxf(A.m[1], mx1 * c);
+  const float b0 = (mn0 == -INFINITY) ? 0.f : mn0, b1 = (mn1 == -INFINITY) ? 0.f : mn1;
+  const float al0 = exp2_approx(A.m[0] - b0), al1 = exp2_approx(A.m[1] - b1);
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) {
+    sc[mt][0] = exp2_approx(fmaf(sc[mt][0], c, -b0));
+    sc[mt][1] = exp2_approx(fmaf(sc[mt][1], c, -b1));
+    sc[mt][2] = exp2_approx(fmaf(sc[mt][2], c, -b0));
+    sc[mt][3] = exp2_approx(fmaf(sc[mt][3], c, -b1));
+    s0 += sc[mt][0] + sc[mt][2];
+    s1 += sc[mt][1] + sc[mt][3];
+  }
+  A.l[0] = A.l[0] * al0 + s0;
+  A.l[1] = A.l[1] * al1 + s1;
+  A.m[0] = mn0;
+  A.m[1] = mn1;
+  if (al0 != 1.f || al1 != 1.f) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      A.o[i][0] *= al0; A.o[i][2] *= al0;
+      A.o[i][1] *= al1; A.o[i][3] *= al1;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      A.ones[i][0] *= al0; A.ones[i][2] *= al0;
+      A.ones[i][1] *= al1; A.ones[i][3] *= al1;
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------- key decode
+// Fast path: default format (level-1 and deep both 4-bit, split_dim 64, float16 radii).
+// Writes the 16 decoded pairs [16t, 16t+16) of stage row `r` as half2 (x, y).
+__device__ __forceinline__ void decode_row_fast(const uint8_t* stage, const AttnParams& P, const uint32_t* lut,
+                                                int r, int t, uint32_t (&kp)[16]) {
+  const uint4 R0 = lds128(stage + swz128(r, 2 * t));
+  const uint4 R1 = lds128(stage + swz128(r, 2 * t + 1));
+  const uint8_t* cp = (t < 2) ? stage + P.off_l1 + r * 16 + 8 * t : stage + P.off_deep + r * 16 + 8 * (t - 2);
+  const uint2 C = lds64(cp);
+  const uint32_t rw[8] = {R0.x, R0.y, R0.z, R0.w, R1.x, R1.y, R1.z, R1.w};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t cw = (i < 8) ? C.x : C.y;
+    const int sh = 4 * (i & 7);
+    const uint32_t cs = lut[(cw >> sh) & 15u];
+    const uint32_t rr = (i & 1) ? bcast_hi(rw[i >> 1]) : bcast_lo(rw[i >> 1]);
+    kp[i] = hmul2u(rr, cs);
+  }
+}
+
+// General path: any supported format.  LUTs: level-1 at lut[0..255], deep at lut[256..511].
+__device__ __forceinline__ void decode_row_general(const uint8_t* stage, const AttnParams& P, const uint32_t* lut,
+                                                   float radius_scale, int r, int t, uint32_t (&kp)[16]) {
+  const uint8_t* l1row = stage + P.off_l1 + r * P.l1_row;
+  const uint8_t* deeprow = stage + P.off_deep + r * P.deep_row;
+#pragma unroll 4
+  for (int i = 0; i < 16; ++i) {
+    const int j = 16 * t + i;
+    uint32_t code, cs;
+    if (j < P.l1_pairs) {
+      if (P.l1_bits == 8) code = l1row[j];
+      else code = (l1row[j >> 1] >> (4 * (j & 1))) & 15u;
+      cs = lut[code];
+    } else {
+      const int rel = j - P.l1_pairs;
+      if (P.deep_bits == 8) code = deeprow[rel];
+      else if (P.deep_bits == 4) code = (deeprow[rel >> 1] >> (4 * (rel & 1))) & 15u;
+      else code = (deeprow[rel >> 2] >> (2 * (rel & 3))) & 3u;
+      cs = lut[kLutEntries + code];
+    }
+    float rad;
+    if (P.int8_radii) {
+      const int8_t rc = reinterpret_cast<const int8_t*>(stage)[r * 64 + j];
+      rad = __expf(float(rc) * radius_scale);
+    } else {
+      rad = __half2float(reinterpret_cast<const __half*>(stage + swz128(r, j >> 3))[j & 7]);
+    }
+    const __half2 h = u32_as_h2(cs);
+    kp[i] = pack_h2(rad * __low2float(h), rad * __high2float(h));
+  }
+}
+
+// ----------------------------------------------------------------------------- one page
+template <bool kFast>
+__device__ __forceinline__ void process_page(WarpAcc& A, const uint8_t* stage, const AttnParams& P, const uint32_t* lut,
+                                             const uint32_t (&qf)[16], float radius_scale, int valid_tokens, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  float sc[4][4];
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) {
+    uint32_t k0[16], k1[16];
+    if (kFast) {
+      decode_row_fast(stage, P, lut, 16 * mt + g, t, k0);
+      decode_row_fast(stage, P, lut, 16 * mt + g + 8, t, k1);
+    } else {
+      decode_row_general(stage, P, lut, radius_scale, 16 * mt + g, t, k0);
+      decode_row_general(stage, P, lut, radius_scale, 16 * mt + g + 8, t, k1);
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) mma16816(acc, k0[2 * ks], k1[2 * ks], k0[2 * ks + 1], k1[2 * ks + 1], qf[2 * ks], qf[2 * ks + 1]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sc[mt][j] = acc[j];
+  }
+  if (valid_tokens < kPage) {
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      if (16 * mt + g >= valid_tokens) sc[mt][0] = sc[mt][1] = -INFINITY;
+      if (16 * mt + g + 8 >= valid_tokens) sc[mt][2] = sc[mt][3] = -INFINITY;
+    }
+  }
+  softmax_update(A, sc, P.scale_log2);
+  const uint8_t* vcodes = stage + P.off_vcodes;
+  const uint8_t* vscales = stage + P.off_vscales;
+  const uint32_t kOne = 0x3C003C00u;
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) {
+    const uint32_t b0 = movmatrix_trans(pack_h2(sc[mt][0], sc[mt][1]));
+    const uint32_t b1 = movmatrix_trans(pack_h2(sc[mt][2], sc[mt][3]));
+    const int tau0 = 16 * mt + 2 * t;
+    const uint4 S01 = lds128(vscales + tau0 * 8);
+    const uint4 S89 = lds128(vscales + (tau0 + 8) * 8);
+#pragma unroll
+    for (int G = 0; G < 4; ++G) {
+      const uint32_t sel = (G & 1) ? 0x7632u : 0x5410u;
+      const uint32_t sA = prmt(G < 2 ? S01.x : S01.y, G < 2 ? S01.z : S01.w, sel);
+      const uint32_t sB = prmt(G < 2 ? S89.x : S89.y, G < 2 ? S89.z : S89.w, sel);
+      const uint32_t bg0 = hmul2u(b0, sA), bg1 = hmul2u(b1, sB);
+      const int chunk = 2 * G + (g >> 2), within = 4 * (g & 3);
+      const uint32_t w0 = lds32(vcodes + tau0 * 128 + (((chunk ^ (tau0 & 7))) << 4) + within);
+      const uint32_t w1 = lds32(vcodes + (tau0 + 1) * 128 + (((chunk ^ ((tau0 + 1) & 7))) << 4) + within);
+      const uint32_t w2 = lds32(vcodes + (tau0 + 8) * 128 + (((chunk ^ ((tau0 + 8) & 7))) << 4) + within);
+      const uint32_t w3 = lds32(vcodes + (tau0 + 9) * 128 + (((chunk ^ ((tau0 + 9) & 7))) << 4) + within);
+      const uint32_t xl01 = prmt(w0, w1, 0x5140) ^ 0x80808080u, xh01 = prmt(w0, w1, 0x7362) ^ 0x80808080u;
+      const uint32_t xl23 = prmt(w2, w3, 0x5140) ^ 0x80808080u, xh23 = prmt(w2, w3, 0x7362) ^ 0x80808080u;
+      const uint32_t K = 0x64646464u;
+      mma16816(A.o[2 * G], prmt(xl01, K, 0x4140), prmt(xl01, K, 0x4342), prmt(xl23, K, 0x4140), prmt(xl23, K, 0x4342), bg0, bg1);
+      mma16816(A.o[2 * G + 1], prmt(xh01, K, 0x4140), prmt(xh01, K, 0x4342), prmt(xh23, K, 0x4140), prmt(xh23, K, 0x4342), bg0, bg1);
+      mma16816(A.ones[G], kOne, kOne, kOne, kOne, bg0, bg1);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------- dense tail
+__device__ __forceinline__ void load_tail_pairs(const void* base, int f32, int64_t row_elem, int col0, int n_pairs,
+                                                bool valid, uint32_t* dst) {
+  if (!valid) {
+    for (int i = 0; i < n_pairs; ++i) dst[i] = 0u;
+    return;
+  }
+  if (f32) {
+    const float2* p = reinterpret_cast<const float2*>(static_cast<const float*>(base) + row_elem + col0);
+    for (int i = 0; i < n_pairs; ++i) {
+      const float2 v = p[i];
+      dst[i] = pack_h2(v.x, v.y);
+    }
+  } else {
+    const uint32_t* p = reinterpret_cast<const uint32_t*>(static_cast<const __half*>(base) + row_elem + col0);
+    for (int i = 0; i < n_pairs; ++i) dst[i] = p[i];
+  }
+}
+
+__device__ void process_tail(WarpAcc& A, const AttnParams& P, int kvh, const uint32_t (&qf)[16], int valid_tokens,
+                             int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  const int64_t head0 = int64_t(kvh) * kPage * kD;
+  float sc[4][4];
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) {
+    uint32_t k0[16], k1[16];
+    const int r0 = 16 * mt + g, r1 = r0 + 8;
+    load_tail_pairs(P.tail_k, P.tail_f32, head0 + int64_t(r0) * kD, 32 * t, 16, r0 < valid_tokens, k0);
+    load_tail_pairs(P.tail_k, P.tail_f32, head0 + int64_t(r1) * kD, 32 * t, 16, r1 < valid_tokens, k1);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) mma16816(acc, k0[2 * ks], k1[2 * ks], k0[2 * ks + 1], k1[2 * ks + 1], qf[2 * ks], qf[2 * ks + 1]);
+    sc[mt][0] = r0 < valid_tokens ? acc[0] : -INFINITY;
+    sc[mt][1] = r0 < valid_tokens ? acc[1] : -INFINITY;
+    sc[mt][2] = r1 < valid_tokens ? acc[2] : -INFINITY;
+    sc[mt][3] = r1 < valid_tokens ? acc[3] : -INFINITY;
+  }
+  softmax_update(A, sc, P.scale_log2);
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) {
+    const uint32_t b0 = movmatrix_trans(pack_h2(sc[mt][0], sc[mt][1]));
+    const uint32_t b1 = movmatrix_trans(pack_h2(sc[mt][2], sc[mt][3]));
+    const int tau[4] = {16 * mt + 2 * t, 16 * mt + 2 * t + 1, 16 * mt + 2 * t + 8, 16 * mt + 2 * t + 9};
+#pragma unroll
+    for (int G = 0; G < 4; ++G) {
+      uint32_t w[4][2];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        load_tail_pairs(P.tail_v, P.tail_f32, head0 + int64_t(tau[i]) * kD, 32 * G + 4 * g, 2, tau[i] < valid_tokens, w[i]);
+      // w[i][0] = (d0, d1), w[i][1] = (d2, d3) of token tau[i].
+      mma16816(A.o[2 * G], prmt(w[0][0], w[1][0], 0x5410), prmt(w[0][0], w[1][0], 0x7632),
+               prmt(w[2][0], w[3][0], 0x5410), prmt(w[2][0], w[3][0], 0x7632), b0, b1);
+      mma16816(A.o[2 * G + 1], prmt(w[0][1], w[1][1], 0x5410), prmt(w[0][1], w[1][1], 0x7632),
+               prmt(w[2][1], w[3][1], 0x5410), prmt(w[2][1], w[3][1], 0x7632), b0, b1);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------- staging
+__device__ __forceinline__ void issue_page(uint8_t* stage, const AttnParams& P, int kvh, int page, int lane) {
+  const int64_t slot = int64_t(kvh) * P.page_capacity + page;
+  // Radii: swizzled 128-byte rows (fp16) or plain 64-byte rows (int8).
+  const uint8_t* rg = P.radii + slot * P.radii_page;
+  const int rchunks = P.radii_page >> 4;
+  if (P.radii_row == 128) {
+    for (int i = lane; i < rchunks; i += 32) cp_async16(stage + swz128(i >> 3, i & 7), rg + (i << 4));
+  } else {
+    for (int i = lane; i < rchunks; i += 32) cp_async16(stage + (i << 4), rg + (i << 4));
+  }
+  const uint8_t* vg = reinterpret_cast<const uint8_t*>(P.v_codes) + slot * kVCodesPage;
+  uint8_t* vs = stage + P.off_vcodes;
+#pragma unroll 4
+  for (int i = lane; i < 512; i += 32) cp_async16(vs + swz128(i >> 3, i & 7), vg + (i << 4));
+  const uint8_t* lg = P.l1 + slot * P.l1_page;
+  for (int i = lane; i < (P.l1_page >> 4); i += 32) cp_async16(stage + P.off_l1 + (i << 4), lg + (i << 4));
+  const uint8_t* dg = P.deep + slot * P.deep_page;
+  for (int i = lane; i < (P.deep_page >> 4); i += 32) cp_async16(stage + P.off_deep + (i << 4), dg + (i << 4));
+  const uint8_t* sg = reinterpret_cast<const uint8_t*>(P.v_scales) + slot * kVScalesPage;
+  cp_async16(stage + P.off_vscales + (lane << 4), sg + (lane << 4));
+}
+
+__device__ __forceinline__ void load_q_frags(const AttnParams& P, int qh_base, int gc, int lane, uint32_t (&qf)[16]) {
+  const int g = lane >> 2, t = lane & 3;
+  if (g < gc) {
+    const int64_t row = int64_t(qh_base + g) * kD + 32 * t;
+    if (P.q_f32) {
+      const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(P.q) + row);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 v = p[i];
+        qf[2 * i] = pack_h2(v.x, v.y);
+        qf[2 * i + 1] = pack_h2(v.z, v.w);
+      }
+    } else {
+      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const __half*>(P.q) + row);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 v = p[i];
+        qf[4 * i] = v.x; qf[4 * i + 1] = v.y; qf[4 * i + 2] = v.z; qf[4 * i + 3] = v.w;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) qf[i] = 0u;
+  }
+}
+
+// Write this warp's partial (m, l, o) for the heads < gc to a [kMaxHeads][130] record.
+__device__ __forceinline__ void store_warp_partial(WarpAcc& A, float* rec, int gc, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  float l0 = A.l[0], l1 = A.l[1];
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+  }
+  const int h0 = 2 * t, h1 = 2 * t + 1;
+#pragma unroll
+  for (int md = 0; md < 8; ++md) {
+    const int G = md >> 1;
+    const int d = 32 * G + 4 * g + 2 * (md & 1);
+    const float c0 = 1152.f * A.ones[G][0], c1 = 1152.f * A.ones[G][1];
+    if (h0 < gc) {
+      rec[h0 * TP_PARTIAL_FLOATS + 2 + d] = A.o[md][0] - c0;
+      rec[h0 * TP_PARTIAL_FLOATS + 3 + d] = A.o[md][2] - c0;
+    }
+    if (h1 < gc) {
+      rec[h1 * TP_PARTIAL_FLOATS + 2 + d] = A.o[md][1] - c1;
+      rec[h1 * TP_PARTIAL_FLOATS + 3 + d] = A.o[md][3] - c1;
+    }
+  }
+  if (g == 0) {
+    if (h0 < gc) { rec[h0 * TP_PARTIAL_FLOATS] = A.m[0]; rec[h0 * TP_PARTIAL_FLOATS + 1] = l0; }
+    if (h1 < gc) { rec[h1 * TP_PARTIAL_FLOATS] = A.m[1]; rec[h1 * TP_PARTIAL_FLOATS + 1] = l1; }
+  }
+}
+
+__device__ __forceinline__ void store_empty_partial(float* rec, int gc, int lane) {
+  for (int i = lane; i < gc * TP_PARTIAL_FLOATS; i += 32) rec[i] = (i % TP_PARTIAL_FLOATS == 0) ? -INFINITY : 0.f;
+}
+
+// Final write of one head's merged (m, l, o[d]) by thread d.
+__device__ __forceinline__ void write_result(const AttnParams& P, int qh, int d, float m, float l, float o) {
+  if (P.partial_out) {
+    float* rec = P.partial_out + int64_t(qh) * TP_PARTIAL_FLOATS;
+    if (d == 0) { rec[0] = m; rec[1] = l; }
+    rec[2 + d] = o;
+  } else {
+    P.out[int64_t(qh) * kD + d] = __float2half_rn(l > 0.f ? o / l : 0.f);
+  }
+}
+
+// ----------------------------------------------------------------------------- kernel
+template <bool kFast>
+__global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __grid_constant__ AttnParams P) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint32_t* lut = reinterpret_cast<uint32_t*>(smem);
+  float* merge = reinterpret_cast<float*>(smem + P.smem_merge_off);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  tp_state st = P.st;
+  if (P.d_state) {
+    st.n_pages = P.d_state[0];
+    st.tail_len = P.d_state[1];
+    st.seq_len = P.d_state[2];
+    st.first_page = P.d_state[3];
+  }
+  const int n_pages = min(max(st.n_pages, 0), P.page_capacity);
+  const int tail_len = min(max(st.tail_len, 0), kPage);
+  const int uph = n_pages + (tail_len > 0 ? 1 : 0);
+  const int VH = P.num_kv_heads * P.nqc;
+  const int64_t U = int64_t(VH) * uph;
+  if (U == 0) {
+    for (int vh = blockIdx.x; vh < VH; vh += gridDim.x) {
+      const int kvh = vh / P.nqc, chunk = vh % P.nqc;
+      const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
+      for (int h = 0; h < gc; ++h) write_result(P, kvh * P.group + chunk * kMaxHeads + h, tid, -INFINITY, 0.f, 0.f);
+    }
+    return;
+  }
+  const int C = int(U < int64_t(gridDim.x) ? U : int64_t(gridDim.x));
+  const int c = blockIdx.x;
+  if (c >= C) return;
+  auto ubeg = [&](int cc) { return int64_t(cc) * U / C; };
+  auto owner = [&](int64_t u) { return int(((u + 1) * C - 1) / U); };
+  const int64_t u0 = ubeg(c), u1 = ubeg(c + 1);
+
+  // Code tables: half2 (cos, sin) of the decoder angle code/(2^bits-1)*2pi - pi, in float32
+  // (rfsn_v11/quant/polar/decoder.py:36-56).
+  for (int i = tid; i < 2 * kLutEntries; i += kThreads) {
+    const int bits = (i < kLutEntries) ? P.l1_bits : P.deep_bits;
+    const int code = i & (kLutEntries - 1);
+    const int lm1 = (1 << bits) - 1;
+    uint32_t v = 0;
+    if (code <= lm1) {
+      const float norm = __fdiv_rn(float(code), float(lm1));
+      const float ang = __fsub_rn(__fmul_rn(norm, 6.28318530717958647692f), 3.14159265358979323846f);
+      v = pack_h2(d2f(cos(double(ang))), d2f(sin(double(ang))));
+    }
+    lut[i] = v;
+  }
+  __syncthreads();
+
+  // Segments of this CTA (at most two heads).
+  const int vh_first = int(u0 / uph), vh_last = int((u1 - 1) / uph);
+  const int nseg = vh_last - vh_first + 1;
+  int seg_a[2], seg_n[2];
+  for (int s = 0; s < 2; ++s) {
+    seg_a[s] = seg_n[s] = 0;
+    if (s < nseg) {
+      const int64_t hb = int64_t(vh_first + s) * uph;
+      const int64_t a = max(u0, hb), b = min(u1, hb + uph);
+      seg_a[s] = int(a - hb);
+      seg_n[s] = int(b - a);
+    }
+  }
+  // This warp's slice of each segment.
+  int wa[2], wn[2];
+  for (int s = 0; s < 2; ++s) {
+    const int lo = seg_a[s] + (warp * seg_n[s]) / kWarps;
+    const int hi = seg_a[s] + ((warp + 1) * seg_n[s]) / kWarps;
+    wa[s] = lo;
+    wn[s] = hi - lo;
+  }
+  const int total = wn[0] + wn[1];
+  uint8_t* stages = smem + P.smem_stage_off + warp * 2 * P.stage_bytes;
+
+  auto unit_of = [&](int i, int& seg, int& j) {
+    if (i < wn[0]) { seg = 0; j = wa[0] + i; }
+    else { seg = 1; j = wa[1] + i - wn[0]; }
+  };
+  auto issue = [&](int i) {
+    if (i < total) {
+      int seg, j;
+      unit_of(i, seg, j);
+      if (j < n_pages) issue_page(stages + (i & 1) * P.stage_bytes, P, (vh_first + seg) / P.nqc, j, lane);
+    }
+    cp_async_commit();
+  };
+
+  issue(0);
+  issue(1);
+  WarpAcc A;
+  uint32_t qf[16];
+  for (int s = 0; s < nseg; ++s) {
+    const int vh = vh_first + s;
+    const int kvh = vh / P.nqc, chunk = vh % P.nqc;
+    const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
+    float* rec = merge + (s * kWarps + warp) * kPartialStride;
+    if (wn[s] == 0) {
+      store_empty_partial(rec, gc, lane);
+      continue;
+    }
+    load_q_frags(P, kvh * P.group + chunk * kMaxHeads, gc, lane, qf);
+    acc_reset(A);
+    const int i0 = (s == 0) ? 0 : wn[0];
+    for (int i = i0; i < i0 + wn[s]; ++i) {
+      if (i + 1 < total) cp_async_wait<1>();
+      else cp_async_wait<0>();
+      __syncwarp();
+      const int j = wa[s] + (i - i0);
+      if (j < n_pages) {
+        const int64_t abs_page = int64_t(st.first_page) + j;
+        const int64_t valid = int64_t(st.seq_len) - abs_page * kPage;
+        const int vt = int(clamp64(valid, 0, kPage));
+        float rs = 0.f;
+        if (P.int8_radii) rs = __half2float(P.radii_scales[int64_t(kvh) * P.page_capacity + j]);
+        process_page<kFast>(A, stages + (i & 1) * P.stage_bytes, P, lut, qf, rs, vt, lane);
+      } else {
+        const int64_t pos0 = (int64_t(st.first_page) + n_pages) * kPage;
+        const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, tail_len));
+        process_tail(A, P, kvh, qf, vt, lane);
+      }
+      __syncwarp();
+      issue(i + 2);
+    }
+    store_warp_partial(A, rec, gc, lane);
+  }
+  __syncthreads();
+
+  // Merge the warps of each segment; write the result or a CTA partial.
+  __shared__ int s_last;
+  for (int s = 0; s < nseg; ++s) {
+    const int vh = vh_first + s;
+    const int kvh = vh / P.nqc, chunk = vh % P.nqc;
+    const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
+    const int qh0 = kvh * P.group + chunk * kMaxHeads;
+    const int c_lo = owner(int64_t(vh) * uph), c_hi = owner(int64_t(vh) * uph + uph - 1);
+    const bool alone = (c_lo == c_hi);
+    float* slot = P.ws_partials + int64_t(c * 2 + s) * kPartialStride;
+    for (int h = 0; h < gc; ++h) {
+      float M = -INFINITY;
+      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, merge[((s * kWarps + w) * kMaxHeads + h) * TP_PARTIAL_FLOATS]);
+      float L = 0.f, O = 0.f;
+      if (M != -INFINITY) {
+        for (int w = 0; w < kWarps; ++w) {
+          const float* r = merge + ((s * kWarps + w) * kMaxHeads + h) * TP_PARTIAL_FLOATS;
+          if (r[0] == -INFINITY) continue;
+          const float f = exp2_approx(r[0] - M);
+          L += r[1] * f;
+          O += r[2 + tid] * f;
+        }
+      }
+      if (alone) {
+        write_result(P, qh0 + h, tid, M, L, O);
+      } else {
+        float* rec = slot + h * TP_PARTIAL_FLOATS;
+        if (tid == 0) { rec[0] = M; rec[1] = L; }
+        rec[2 + tid] = O;
+      }
+    }
+    if (alone) continue;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const int prev = atomicAdd(&P.ws_counters[vh], 1);
+      s_last = (prev == c_hi - c_lo);
+      if (s_last) P.ws_counters[vh] = 0;
+    }
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      for (int h = 0; h < gc; ++h) {
+        float M = -INFINITY;
+        for (int cc = c_lo; cc <= c_hi; ++cc) {
+          const int sc = vh - int(ubeg(cc) / uph);
+          M = fmaxf(M, __ldcg(P.ws_partials + int64_t(cc * 2 + sc) * kPartialStride + h * TP_PARTIAL_FLOATS));
+        }
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+          for (int cc = c_lo; cc <= c_hi; ++cc) {
+            const int sc = vh - int(ubeg(cc) / uph);
+            const float* r = P.ws_partials + int64_t(cc * 2 + sc) * kPartialStride + h * TP_PARTIAL_FLOATS;
+            const float m = __ldcg(r);
+            if (m == -INFINITY) continue;
+            const float f = exp2_approx(m - M);
+            L += __ldcg(r + 1) * f;
+            O += __ldcg(r + 2 + tid) * f;
+          }
+        }
+        write_result(P, qh0 + h, tid, M, L, O);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ----------------------------------------------------------------------------- cross-shard combine
+__global__ void combine_kernel(const float* partials, int n_parts, int num_q_heads, __half* out) {
+  const int h = blockIdx.x, d = threadIdx.x;
+  float M = -INFINITY;
+  for (int r = 0; r < n_parts; ++r) M = fmaxf(M, partials[(int64_t(r) * num_q_heads + h) * TP_PARTIAL_FLOATS]);
+  float L = 0.f, O = 0.f;
+  if (M != -INFINITY) {
+    for (int r = 0; r < n_parts; ++r) {
+      const float* rec = partials + (int64_t(r) * num_q_heads + h) * TP_PARTIAL_FLOATS;
+      if (rec[0] == -INFINITY) continue;
+      const float f = exp2f(rec[0] - M);
+      L += rec[1] * f;
+      O += rec[2 + d] * f;
+    }
+  }
+  out[int64_t(h) * kD + d] = __float2half_rn(L > 0.f ? O / L : 0.f);
+}
+
+static int g_num_sms = 0;
+
+static int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_num_sms = n;
+  }
+  return g_num_sms;
+}
+
+static int grid_size(int num_kv_heads, int num_q_heads) {
+  const int group = num_q_heads / num_kv_heads;
+  const int nqc = (group + kMaxHeads - 1) / kMaxHeads;
+  return max(num_sms(), num_kv_heads * nqc);
+}
+
+}  // namespace tp
+
+using namespace tp;
+
+extern "C" {
+
+size_t tp_decode_attention_workspace_size(int32_t num_kv_heads, int32_t num_q_heads) {
+  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads) return 0;
+  const int grid = grid_size(num_kv_heads, num_q_heads);
+  const int vh = num_kv_heads * ((num_q_heads / num_kv_heads + kMaxHeads - 1) / kMaxHeads);
+  size_t bytes = size_t(grid) * 2 * kPartialStride * sizeof(float);
+  bytes = (bytes + 255) & ~size_t(255);
+  bytes += size_t(vh) * sizeof(int);
+  return (bytes + 255) & ~size_t(255);
+}
+
+int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state state, const int32_t* d_state,
+                        const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
+                        float* partial_out, void* workspace, size_t workspace_bytes, void* stream) {
+  Layout L;
+  int st = validate_pool(pool, &L);
+  if (st != TP_OK) return st;
+  const int hkv = pool->num_kv_heads;
+  if (num_q_heads <= 0 || num_q_heads % hkv)
+    return fail(TP_ERR_INVALID, "num_q_heads must be divisible by num_kv_heads for GQA");
+  if (!q) return fail(TP_ERR_INVALID, "tp_decode_attention: q is NULL");
+  if (q_dtype != TP_F16 && q_dtype != TP_F32) return fail(TP_ERR_INVALID, "q must be float16 or float32");
+  if (!out && !partial_out) return fail(TP_ERR_INVALID, "tp_decode_attention: no output buffer");
+  if (!(scale > 0.f)) return fail(TP_ERR_INVALID, "attention scale must be positive");
+  if (!d_state) {
+    if (state.n_pages < 0 || state.n_pages > pool->page_capacity)
+      return fail(TP_ERR_INVALID, "n_pages outside the page pool");
+    if (state.tail_len < 0 || state.tail_len > TP_PAGE_TOKENS) return fail(TP_ERR_INVALID, "tail_len must be in [0, 64]");
+    if (state.n_pages == 0 && state.tail_len == 0) return fail(TP_ERR_INVALID, "attention over an empty cache");
+  }
+  if (!tail || ((d_state || state.tail_len > 0) && (!tail->k || !tail->v)))
+    return fail(TP_ERR_INVALID, "tp_decode_attention: tail buffers missing");
+  const size_t need = tp_decode_attention_workspace_size(hkv, num_q_heads);
+  if (!workspace || workspace_bytes < need)
+    return fail(TP_ERR_INVALID, "tp_decode_attention: workspace too small (need " + std::to_string(need) + " bytes)");
+  if ((reinterpret_cast<uintptr_t>(q) & 15)) return fail(TP_ERR_INVALID, "q must be 16-byte aligned");
+
+  AttnParams P;
+  P.radii = static_cast<const uint8_t*>(pool->radii);
+  P.radii_scales = static_cast<const __half*>(pool->radii_scales);
+  P.l1 = static_cast<const uint8_t*>(pool->angle_codes_l1);
+  P.deep = static_cast<const uint8_t*>(pool->angle_codes_deep);
+  P.v_codes = static_cast<const int8_t*>(pool->v_codes);
+  P.v_scales = static_cast<const __half*>(pool->v_scales);
+  P.page_capacity = pool->page_capacity;
+  P.l1_bits = pool->fmt.l1_bits;
+  P.deep_bits = pool->fmt.deep_bits;
+  P.l1_pairs = L.l1_pairs;
+  P.l1_row = L.l1_row;
+  P.deep_row = L.deep_row;
+  P.radii_row = L.radii_row;
+  P.int8_radii = pool->fmt.int8_radii;
+  P.radii_page = int(L.radii_page);
+  P.l1_page = int(L.l1_page);
+  P.deep_page = int(L.deep_page);
+  P.tail_k = tail->k;
+  P.tail_v = tail->v;
+  P.tail_f32 = tail->dtype == TP_F32;
+  P.st = state;
+  P.d_state = d_state;
+  P.q = q;
+  P.q_f32 = q_dtype == TP_F32;
+  P.num_q_heads = num_q_heads;
+  P.num_kv_heads = hkv;
+  P.group = num_q_heads / hkv;
+  P.nqc = (P.group + kMaxHeads - 1) / kMaxHeads;
+  P.scale_log2 = scale * 1.4426950408889634f;
+  P.out = static_cast<__half*>(out);
+  P.partial_out = partial_out;
+  const int grid = grid_size(hkv, num_q_heads);
+  P.ws_partials = static_cast<float*>(workspace);
+  size_t part_bytes = (size_t(grid) * 2 * kPartialStride * sizeof(float) + 255) & ~size_t(255);
+  P.ws_counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + part_bytes);
+  // Stage layout: radii | v codes | level-1 codes | 64-byte bank shift | deep codes | v scales.
+  auto up = [](int x, int a) { return (x + a - 1) / a * a; };
+  P.off_vcodes = P.radii_page;
+  P.off_l1 = P.off_vcodes + int(kVCodesPage);
+  P.off_deep = P.off_l1 + up(P.l1_page, 128) + 64;
+  P.off_vscales = up(P.off_deep + P.deep_page, 128);
+  P.stage_bytes = up(P.off_vscales + int(kVScalesPage), 128);
+  P.smem_merge_off = 2 * kLutEntries * 4;
+  P.smem_stage_off = P.smem_merge_off + 2 * kWarps * kPartialStride * int(sizeof(float));
+  const int smem = P.smem_stage_off + kWarps * 2 * P.stage_bytes;
+
+  const bool fast = P.l1_bits == 4 && P.deep_bits == 4 && pool->fmt.split_dim == 64 && !P.int8_radii;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (fast) {
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(decode_attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      attr = true;
+    }
+    decode_attention_kernel<true><<<grid, kThreads, smem, s>>>(P);
+  } else {
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(decode_attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      attr = true;
+    }
+    decode_attention_kernel<false><<<grid, kThreads, smem, s>>>(P);
+  }
+  return check_launch("tp_decode_attention");
+}
+
+int tp_combine_partials(const float* partials, int32_t n_parts, int32_t num_q_heads, void* out, void* stream) {
+  if (!partials || !out || n_parts <= 0 || num_q_heads <= 0) return fail(TP_ERR_INVALID, "tp_combine_partials: bad argument");
+  combine_kernel<<<num_q_heads, kD, 0, static_cast<cudaStream_t>(stream)>>>(partials, n_parts, num_q_heads,
+                                                                             static_cast<__half*>(out));
+  return check_launch("tp_combine_partials");
+}
+
+}  // extern "C"

@@ -1,0 +1,171 @@
+// Secondary kernels: scores-only attention and page decompression.
+#include "tp_common.cuh"
+
+namespace tp {
+
+
+struct PageView {
+  const uint8_t* radii;
+  const __half* radii_scales;
+  const uint8_t* l1;
+  const uint8_t* deep;
+  const int8_t* v_codes;
+  const __half* v_scales;
+  int page_capacity, l1_bits, deep_bits, l1_pairs, l1_row, deep_row, radii_row, int8_radii;
+};
+
+static PageView page_view(const tp_page_pool& p, const Layout& L) {
+  PageView v;
+  v.radii = static_cast<const uint8_t*>(p.radii);
+  v.radii_scales = static_cast<const __half*>(p.radii_scales);
+  v.l1 = static_cast<const uint8_t*>(p.angle_codes_l1);
+  v.deep = static_cast<const uint8_t*>(p.angle_codes_deep);
+  v.v_codes = static_cast<const int8_t*>(p.v_codes);
+  v.v_scales = static_cast<const __half*>(p.v_scales);
+  v.page_capacity = p.page_capacity;
+  v.l1_bits = p.fmt.l1_bits;
+  v.deep_bits = p.fmt.deep_bits;
+  v.l1_pairs = L.l1_pairs;
+  v.l1_row = L.l1_row;
+  v.deep_row = L.deep_row;
+  v.radii_row = L.radii_row;
+  v.int8_radii = p.fmt.int8_radii;
+  return v;
+}
+
+// float32 (cos, sin) of every code of both code sets; the decoder's angle formula in float32
+// (rfsn_v11/quant/polar/decoder.py:36-56).
+__device__ void build_cos_sin(float2* tab, int l1_bits, int deep_bits) {
+  for (int i = threadIdx.x; i < 512; i += blockDim.x) {
+    const int bits = i < 256 ? l1_bits : deep_bits;
+    const int code = i & 255, lm1 = (1 << bits) - 1;
+    float2 v = make_float2(0.f, 0.f);
+    if (code <= lm1) {
+      const float norm = __fdiv_rn(float(code), float(lm1));
+      const float ang = __fsub_rn(__fmul_rn(norm, 6.28318530717958647692f), 3.14159265358979323846f);
+      v = make_float2(d2f(cos(double(ang))), d2f(sin(double(ang))));
+    }
+    tab[i] = v;
+  }
+}
+
+// Decoded float16 key pair j of token l of one page: fp16(r * cos), fp16(r * sin) with the
+// float32 products of decoder.py:57-67.
+__device__ __forceinline__ __half2 decode_pair(const PageView& V, const float2* tab, int64_t slot, int l, int j) {
+  uint32_t code;
+  const float2* t;
+  if (j < V.l1_pairs) {
+    const uint8_t* row = V.l1 + (slot * kPage + l) * V.l1_row;
+    code = V.l1_bits == 8 ? row[j] : (row[j >> 1] >> (4 * (j & 1))) & 15u;
+    t = tab;
+  } else {
+    const int rel = j - V.l1_pairs;
+    const uint8_t* row = V.deep + (slot * kPage + l) * V.deep_row;
+    if (V.deep_bits == 8) code = row[rel];
+    else if (V.deep_bits == 4) code = (row[rel >> 1] >> (4 * (rel & 1))) & 15u;
+    else code = (row[rel >> 2] >> (2 * (rel & 3))) & 3u;
+    t = tab + 256;
+  }
+  float r;
+  if (V.int8_radii) {
+    const int8_t rc = reinterpret_cast<const int8_t*>(V.radii)[(slot * kPage + l) * kPairs + j];
+    const float arg = __fmul_rn(float(rc), __half2float(V.radii_scales[slot]));
+    r = d2f(exp(double(arg)));
+  } else {
+    r = __half2float(reinterpret_cast<const __half*>(V.radii)[(slot * kPage + l) * kPairs + j]);
+  }
+  const float2 cs = t[code];
+  return __halves2half2(__float2half_rn(__fmul_rn(r, cs.x)), __float2half_rn(__fmul_rn(r, cs.y)));
+}
+
+// One CTA per (page, KV head); thread l = token.  Scores accumulate in float32 over the
+// float16-rounded decoded key.
+__global__ void fused_scores_kernel(PageView V, const void* q, int q_f32, int num_q_heads, int group, float scale,
+                                    int n_pages, __half* scores) {
+  __shared__ float2 tab[512];
+  __shared__ float qs[8][kD];
+  build_cos_sin(tab, V.l1_bits, V.deep_bits);
+  const int p = blockIdx.x, h = blockIdx.y, l = threadIdx.x;
+  const int64_t slot = int64_t(h) * V.page_capacity + p;
+  for (int g0 = 0; g0 < group; g0 += 8) {
+    const int gc = min(8, group - g0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < gc * kD; i += blockDim.x) {
+      const int64_t idx = int64_t(h * group + g0 + i / kD) * kD + i % kD;
+      qs[i / kD][i % kD] = q_f32 ? __half2float(__float2half_rn(static_cast<const float*>(q)[idx]))
+                                 : __half2float(static_cast<const __half*>(q)[idx]);
+    }
+    __syncthreads();
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < kPairs; ++j) {
+      const float2 k = __half22float2(decode_pair(V, tab, slot, l, j));
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh)
+        if (hh < gc) acc[hh] = fmaf(qs[hh][2 * j], k.x, fmaf(qs[hh][2 * j + 1], k.y, acc[hh]));
+    }
+    for (int hh = 0; hh < gc; ++hh)
+      scores[int64_t(h * group + g0 + hh) * n_pages * kPage + int64_t(p) * kPage + l] = __float2half_rn(acc[hh] * scale);
+  }
+}
+
+// One CTA per (page, KV head), 256 threads: thread (token l, quarter c) writes key pairs
+// [16c, 16c+16) and values [32c, 32c+32) of token l.
+__global__ void decode_pages_kernel(PageView V, int first_page, int n_pages, __half* k_out, __half* v_out) {
+  __shared__ float2 tab[512];
+  build_cos_sin(tab, V.l1_bits, V.deep_bits);
+  __syncthreads();
+  const int p = blockIdx.x, h = blockIdx.y;
+  const int l = threadIdx.x >> 2, c = threadIdx.x & 3;
+  const int64_t slot = int64_t(h) * V.page_capacity + first_page + p;
+  const int64_t orow = (int64_t(h) * n_pages + p) * kPage + l;
+  if (k_out) {
+    __half2* ko = reinterpret_cast<__half2*>(k_out + orow * kD);
+    for (int i = 0; i < 16; ++i) ko[16 * c + i] = decode_pair(V, tab, slot, l, 16 * c + i);
+  }
+  const int8_t* vc = V.v_codes + (slot * kPage + l) * kD + 32 * c;
+  const float s = __half2float(V.v_scales[(slot * kPage + l) * 4 + c]);
+  __half* vo = v_out + orow * kD + 32 * c;
+  for (int i = 0; i < 32; ++i) vo[i] = __float2half_rn(__fmul_rn(float(vc[i]), s));
+}
+
+}  // namespace tp
+
+using namespace tp;
+
+extern "C" {
+
+int tp_fused_scores(const tp_page_pool* pool, int32_t n_pages, const void* q, int32_t q_dtype, int32_t num_q_heads,
+                    float scale, void* scores, void* stream) {
+  Layout L;
+  int st = validate_pool(pool, &L);
+  if (st != TP_OK) return st;
+  if (num_q_heads <= 0 || num_q_heads % pool->num_kv_heads)
+    return fail(TP_ERR_INVALID, "num_q_heads must be divisible by num_kv_heads for GQA");
+  if (n_pages < 0 || n_pages > pool->page_capacity) return fail(TP_ERR_INVALID, "n_pages outside the page pool");
+  if (!q || !scores) return fail(TP_ERR_INVALID, "tp_fused_scores: NULL argument");
+  if (q_dtype != TP_F16 && q_dtype != TP_F32) return fail(TP_ERR_INVALID, "q must be float16 or float32");
+  if (n_pages == 0) return TP_OK;
+  dim3 grid(n_pages, pool->num_kv_heads);
+  fused_scores_kernel<<<grid, kPage, 0, static_cast<cudaStream_t>(stream)>>>(
+      page_view(*pool, L), q, q_dtype == TP_F32, num_q_heads, num_q_heads / pool->num_kv_heads, scale, n_pages,
+      static_cast<__half*>(scores));
+  return check_launch("tp_fused_scores");
+}
+
+int tp_decode_pages(const tp_page_pool* pool, int32_t first_page, int32_t n_pages, void* k_out, void* v_out,
+                    void* stream) {
+  Layout L;
+  int st = validate_pool(pool, &L, k_out != nullptr);
+  if (st != TP_OK) return st;
+  if (first_page < 0 || n_pages < 0 || int64_t(first_page) + n_pages > pool->page_capacity)
+    return fail(TP_ERR_INVALID, "tp_decode_pages: page range outside the pool");
+  if (!v_out) return fail(TP_ERR_INVALID, "tp_decode_pages: NULL value output");
+  if (n_pages == 0) return TP_OK;
+  dim3 grid(n_pages, pool->num_kv_heads);
+  decode_pages_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(page_view(*pool, L), first_page, n_pages,
+                                                                           static_cast<__half*>(k_out),
+                                                                           static_cast<__half*>(v_out));
+  return check_launch("tp_decode_pages");
+}
+
+}  // extern "C"
