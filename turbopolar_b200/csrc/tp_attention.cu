@@ -4,15 +4,16 @@
 // (rfsn_v11/kernels/turbo_polar/tqpolar_online_attention.metal:197-629) with the numerics of
 // the bridge's CPU fallback (rfsn_v11/kernels/turbo_polar/metal.py:293-332) as the target.
 //
-// Work decomposition.  A "unit" is one 64-token page of one (KV head, query chunk), or that
-// head's dense tail.  The units of all heads form one flat list that is cut into gridDim.x
+// Work decomposition.  A "unit" is one half page (32 tokens) of one (KV head, query chunk), or
+// that head's dense tail.  The units of all heads form one flat list cut into gridDim.x
 // contiguous ranges, one per CTA, so every SM streams the same number of pages whatever the
-// head count or context length; a range spans at most two heads ("segments").  Inside a CTA
-// each of the 4 warps takes a contiguous quarter of each segment and streams its pages through
-// a private double buffer in shared memory (cp.async, 16 bytes per lane, rows of radii and
-// value codes XOR-swizzled so the fragment loads below are bank-conflict free).
+// head count or context length; a range spans at most two heads ("segments").  Each of the 8
+// warps of a CTA takes a contiguous slice of each segment and streams exactly the rows it
+// consumes through a private double buffer in shared memory (cp.async, 16 bytes per lane; rows
+// of radii and value codes XOR-swizzled so the fragment loads below are bank-conflict free),
+// so warps never wait on one another inside the loop.
 //
-// Per page a warp computes, with mma.sync m16n8k16 (fp16 in, fp32 accumulate):
+// Per half page a warp computes, with mma.sync m16n8k16 (fp16 in, fp32 accumulate):
 //   S^T[token][head] = K[token][dim] . Q^T[dim][head]      M = 16 tokens, N = 8 query heads
 // where every lane decodes exactly the key pairs its A fragment holds: lane (g, t) owns pairs
 // [16t, 16t+16) of tokens g and g+8, each pair k = radius * (cos, sin)(code) from a 16-entry
@@ -27,17 +28,19 @@
 //
 // Split combine.  Warps of a CTA merge through shared memory; CTAs that share a head write a
 // partial (m, l, o[128]) to the workspace and the last to arrive (atomic ticket per head)
-// merges them and writes the fp16 output, then resets the ticket, all in the same launch.
+// merges them in parallel and writes the fp16 output, then resets the ticket, all in the same
+// launch.
 #include <cfloat>
+#include <cmath>
 
 #include "tp_common.cuh"
 
 namespace tp {
 
-
-constexpr int kWarps = 4;
+constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxHeads = 8;  // query heads per unit (N of the mma)
+constexpr int kHalf = 32;     // tokens per unit
 constexpr int kPartialStride = kMaxHeads * TP_PARTIAL_FLOATS;  // floats per workspace slot
 constexpr int kLutEntries = 256;
 
@@ -58,14 +61,15 @@ struct AttnParams {
   const int32_t* d_state;
   const void* q;
   int q_f32;
-  int num_q_heads, num_kv_heads, group, nqc;
+  int num_q_heads, num_kv_heads, group, nqc, gmax;
   float scale_log2;
   __half* out;
   float* partial_out;
   float* ws_partials;
   int* ws_counters;
   int stage_bytes, off_vcodes, off_l1, off_deep, off_vscales;
-  int smem_merge_off, smem_stage_off;
+  int smem_merge_off, smem_stage_off, scratch_floats;
+  uint32_t lut[2 * kLutEntries];  // half2 (cos, sin) per code: level-1 [0, 256), deep [256, 512)
 };
 
 __device__ __forceinline__ int64_t clamp64(int64_t x, int64_t lo, int64_t hi) { return x < lo ? lo : (x > hi ? hi : x); }
@@ -77,8 +81,6 @@ __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpre
 __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
   return h2_as_u32(__hmul2(u32_as_h2(a), u32_as_h2(b)));
 }
-__device__ __forceinline__ uint32_t bcast_lo(uint32_t w) { return prmt(w, 0, 0x1010); }
-__device__ __forceinline__ uint32_t bcast_hi(uint32_t w) { return prmt(w, 0, 0x3232); }
 
 // Byte offset of 16-byte chunk `c` of row `r` in a swizzled 128-byte-row tile.
 __device__ __forceinline__ int swz128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
@@ -103,11 +105,12 @@ __device__ __forceinline__ void acc_reset(WarpAcc& A) {
   A.l[0] = A.l[1] = 0.f;
 }
 
-// Online-softmax update from the raw score fragments of one 64-token unit; returns P in sc.
-__device__ __forceinline__ void softmax_update(WarpAcc& A, float (&sc)[4][4], float c) {
+// Online-softmax update from the raw score fragments of NT 16-token tiles; returns P in sc.
+template <int NT>
+__device__ __forceinline__ void softmax_update(WarpAcc& A, float (&sc)[NT][4], float c) {
   float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-  for (int mt = 0; mt < 4; ++mt) {
+  for (int mt = 0; mt < NT; ++mt) {
     mx0 = fmaxf(mx0, fmaxf(sc[mt][0], sc[mt][2]));
     mx1 = fmaxf(mx1, fmaxf(sc[mt][1], sc[mt][3]));
   }
@@ -118,10 +121,9 @@ __device__ __forceinline__ void softmax_update(WarpAcc& A, float (&sc)[4][4], fl
   }
   const float mn0 = fmaxf(A.m[0], mx0 * c), mn1 = fmaxf(A.m[1], mx1 * c);
   const float b0 = (mn0 == -INFINITY) ? 0.f : mn0, b1 = (mn1 == -INFINITY) ? 0.f : mn1;
-  const float al0 = exp2_approx(A.m[0] - b0), al1 = exp2_approx(A.m[1] - b1);
   float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-  for (int mt = 0; mt < 4; ++mt) {
+  for (int mt = 0; mt < NT; ++mt) {
     sc[mt][0] = exp2_approx(fmaf(sc[mt][0], c, -b0));
     sc[mt][1] = exp2_approx(fmaf(sc[mt][1], c, -b1));
     sc[mt][2] = exp2_approx(fmaf(sc[mt][2], c, -b0));
@@ -129,11 +131,10 @@ __device__ __forceinline__ void softmax_update(WarpAcc& A, float (&sc)[4][4], fl
     s0 += sc[mt][0] + sc[mt][2];
     s1 += sc[mt][1] + sc[mt][3];
   }
-  A.l[0] = A.l[0] * al0 + s0;
-  A.l[1] = A.l[1] * al1 + s1;
-  A.m[0] = mn0;
-  A.m[1] = mn1;
-  if (al0 != 1.f || al1 != 1.f) {
+  if (mn0 != A.m[0] || mn1 != A.m[1]) {
+    const float al0 = exp2_approx(A.m[0] - b0), al1 = exp2_approx(A.m[1] - b1);
+    A.l[0] *= al0;
+    A.l[1] *= al1;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       A.o[i][0] *= al0; A.o[i][2] *= al0;
@@ -144,7 +145,11 @@ __device__ __forceinline__ void softmax_update(WarpAcc& A, float (&sc)[4][4], fl
       A.ones[i][0] *= al0; A.ones[i][2] *= al0;
       A.ones[i][1] *= al1; A.ones[i][3] *= al1;
     }
+    A.m[0] = mn0;
+    A.m[1] = mn1;
   }
+  A.l[0] += s0;
+  A.l[1] += s1;
 }
 
 // ----------------------------------------------------------------------------- key decode
@@ -162,8 +167,8 @@ __device__ __forceinline__ void decode_row_fast(const uint8_t* stage, const Attn
     const uint32_t cw = (i < 8) ? C.x : C.y;
     const int sh = 4 * (i & 7);
     const uint32_t cs = lut[(cw >> sh) & 15u];
-    const uint32_t rr = (i & 1) ? bcast_hi(rw[i >> 1]) : bcast_lo(rw[i >> 1]);
-    kp[i] = hmul2u(rr, cs);
+    const __half2 rp = u32_as_h2(rw[i >> 1]);
+    kp[i] = h2_as_u32(__hmul2((i & 1) ? __high2half2(rp) : __low2half2(rp), u32_as_h2(cs)));
   }
 }
 
@@ -199,14 +204,14 @@ __device__ __forceinline__ void decode_row_general(const uint8_t* stage, const A
   }
 }
 
-// ----------------------------------------------------------------------------- one page
+// ----------------------------------------------------------------------------- one half page
 template <bool kFast>
-__device__ __forceinline__ void process_page(WarpAcc& A, const uint8_t* stage, const AttnParams& P, const uint32_t* lut,
+__device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, const AttnParams& P, const uint32_t* lut,
                                              const uint32_t (&qf)[16], float radius_scale, int valid_tokens, int lane) {
   const int g = lane >> 2, t = lane & 3;
-  float sc[4][4];
+  float sc[2][4];
 #pragma unroll
-  for (int mt = 0; mt < 4; ++mt) {
+  for (int mt = 0; mt < 2; ++mt) {
     uint32_t k0[16], k1[16];
     if (kFast) {
       decode_row_fast(stage, P, lut, 16 * mt + g, t, k0);
@@ -215,25 +220,28 @@ __device__ __forceinline__ void process_page(WarpAcc& A, const uint8_t* stage, c
       decode_row_general(stage, P, lut, radius_scale, 16 * mt + g, t, k0);
       decode_row_general(stage, P, lut, radius_scale, 16 * mt + g + 8, t, k1);
     }
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) mma16816(acc, k0[2 * ks], k1[2 * ks], k0[2 * ks + 1], k1[2 * ks + 1], qf[2 * ks], qf[2 * ks + 1]);
+    for (int ks = 0; ks < 8; ks += 2) {
+      mma16816(a0, k0[2 * ks], k1[2 * ks], k0[2 * ks + 1], k1[2 * ks + 1], qf[2 * ks], qf[2 * ks + 1]);
+      mma16816(a1, k0[2 * ks + 2], k1[2 * ks + 2], k0[2 * ks + 3], k1[2 * ks + 3], qf[2 * ks + 2], qf[2 * ks + 3]);
+    }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) sc[mt][j] = acc[j];
+    for (int j = 0; j < 4; ++j) sc[mt][j] = a0[j] + a1[j];
   }
-  if (valid_tokens < kPage) {
+  if (valid_tokens < kHalf) {
 #pragma unroll
-    for (int mt = 0; mt < 4; ++mt) {
+    for (int mt = 0; mt < 2; ++mt) {
       if (16 * mt + g >= valid_tokens) sc[mt][0] = sc[mt][1] = -INFINITY;
       if (16 * mt + g + 8 >= valid_tokens) sc[mt][2] = sc[mt][3] = -INFINITY;
     }
   }
-  softmax_update(A, sc, P.scale_log2);
+  softmax_update<2>(A, sc, P.scale_log2);
   const uint8_t* vcodes = stage + P.off_vcodes;
   const uint8_t* vscales = stage + P.off_vscales;
   const uint32_t kOne = 0x3C003C00u;
 #pragma unroll
-  for (int mt = 0; mt < 4; ++mt) {
+  for (int mt = 0; mt < 2; ++mt) {
     const uint32_t b0 = movmatrix_trans(pack_h2(sc[mt][0], sc[mt][1]));
     const uint32_t b1 = movmatrix_trans(pack_h2(sc[mt][2], sc[mt][3]));
     const int tau0 = 16 * mt + 2 * t;
@@ -279,6 +287,7 @@ __device__ __forceinline__ void load_tail_pairs(const void* base, int f32, int64
   }
 }
 
+// The whole dense tail (up to 64 tokens) of KV head kvh, read straight from global memory.
 __device__ void process_tail(WarpAcc& A, const AttnParams& P, int kvh, const uint32_t (&qf)[16], int valid_tokens,
                              int lane) {
   const int g = lane >> 2, t = lane & 3;
@@ -298,7 +307,7 @@ __device__ void process_tail(WarpAcc& A, const AttnParams& P, int kvh, const uin
     sc[mt][2] = r1 < valid_tokens ? acc[2] : -INFINITY;
     sc[mt][3] = r1 < valid_tokens ? acc[3] : -INFINITY;
   }
-  softmax_update(A, sc, P.scale_log2);
+  softmax_update<4>(A, sc, P.scale_log2);
 #pragma unroll
   for (int mt = 0; mt < 4; ++mt) {
     const uint32_t b0 = movmatrix_trans(pack_h2(sc[mt][0], sc[mt][1]));
@@ -320,26 +329,29 @@ __device__ void process_tail(WarpAcc& A, const AttnParams& P, int kvh, const uin
 }
 
 // ----------------------------------------------------------------------------- staging
-__device__ __forceinline__ void issue_page(uint8_t* stage, const AttnParams& P, int kvh, int page, int lane) {
+// Rows [32*half, 32*half + 32) of page `page` of KV head kvh into a half-page stage.
+__device__ __forceinline__ void issue_half(uint8_t* stage, const AttnParams& P, int kvh, int page, int half, int lane) {
   const int64_t slot = int64_t(kvh) * P.page_capacity + page;
-  // Radii: swizzled 128-byte rows (fp16) or plain 64-byte rows (int8).
-  const uint8_t* rg = P.radii + slot * P.radii_page;
-  const int rchunks = P.radii_page >> 4;
+  const int hr = half * kHalf;
+  const uint8_t* rg = P.radii + slot * P.radii_page + hr * P.radii_row;
+  const int rchunks = (kHalf * P.radii_row) >> 4;
   if (P.radii_row == 128) {
+#pragma unroll 2
     for (int i = lane; i < rchunks; i += 32) cp_async16(stage + swz128(i >> 3, i & 7), rg + (i << 4));
   } else {
     for (int i = lane; i < rchunks; i += 32) cp_async16(stage + (i << 4), rg + (i << 4));
   }
-  const uint8_t* vg = reinterpret_cast<const uint8_t*>(P.v_codes) + slot * kVCodesPage;
+  const uint8_t* vg = reinterpret_cast<const uint8_t*>(P.v_codes) + slot * kVCodesPage + hr * kD;
   uint8_t* vs = stage + P.off_vcodes;
-#pragma unroll 4
-  for (int i = lane; i < 512; i += 32) cp_async16(vs + swz128(i >> 3, i & 7), vg + (i << 4));
-  const uint8_t* lg = P.l1 + slot * P.l1_page;
-  for (int i = lane; i < (P.l1_page >> 4); i += 32) cp_async16(stage + P.off_l1 + (i << 4), lg + (i << 4));
-  const uint8_t* dg = P.deep + slot * P.deep_page;
-  for (int i = lane; i < (P.deep_page >> 4); i += 32) cp_async16(stage + P.off_deep + (i << 4), dg + (i << 4));
-  const uint8_t* sg = reinterpret_cast<const uint8_t*>(P.v_scales) + slot * kVScalesPage;
-  cp_async16(stage + P.off_vscales + (lane << 4), sg + (lane << 4));
+#pragma unroll
+  for (int i = lane; i < 256; i += 32) cp_async16(vs + swz128(i >> 3, i & 7), vg + (i << 4));
+  const int l1c = (kHalf * P.l1_row) >> 4, dc = (kHalf * P.deep_row) >> 4;
+  const uint8_t* lg = P.l1 + slot * P.l1_page + hr * P.l1_row;
+  for (int i = lane; i < l1c; i += 32) cp_async16(stage + P.off_l1 + (i << 4), lg + (i << 4));
+  const uint8_t* dg = P.deep + slot * P.deep_page + hr * P.deep_row;
+  for (int i = lane; i < dc; i += 32) cp_async16(stage + P.off_deep + (i << 4), dg + (i << 4));
+  const uint8_t* sg = reinterpret_cast<const uint8_t*>(P.v_scales) + slot * kVScalesPage + hr * 8;
+  if (lane < 16) cp_async16(stage + P.off_vscales + (lane << 4), sg + (lane << 4));
 }
 
 __device__ __forceinline__ void load_q_frags(const AttnParams& P, int qh_base, int gc, int lane, uint32_t (&qf)[16]) {
@@ -368,7 +380,7 @@ __device__ __forceinline__ void load_q_frags(const AttnParams& P, int qh_base, i
   }
 }
 
-// Write this warp's partial (m, l, o) for the heads < gc to a [kMaxHeads][130] record.
+// Write this warp's partial (m, l, o) for the heads < gc to a [gc][130] record.
 __device__ __forceinline__ void store_warp_partial(WarpAcc& A, float* rec, int gc, int lane) {
   const int g = lane >> 2, t = lane & 3;
   float l0 = A.l[0], l1 = A.l[1];
@@ -402,7 +414,7 @@ __device__ __forceinline__ void store_empty_partial(float* rec, int gc, int lane
   for (int i = lane; i < gc * TP_PARTIAL_FLOATS; i += 32) rec[i] = (i % TP_PARTIAL_FLOATS == 0) ? -INFINITY : 0.f;
 }
 
-// Final write of one head's merged (m, l, o[d]) by thread d.
+// Final write of one head's merged (m, l, o[d]).
 __device__ __forceinline__ void write_result(const AttnParams& P, int qh, int d, float m, float l, float o) {
   if (P.partial_out) {
     float* rec = P.partial_out + int64_t(qh) * TP_PARTIAL_FLOATS;
@@ -420,6 +432,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   uint32_t* lut = reinterpret_cast<uint32_t*>(smem);
   float* merge = reinterpret_cast<float*>(smem + P.smem_merge_off);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gmax = P.gmax;
+  const int rec_stride = gmax * TP_PARTIAL_FLOATS;
 
   tp_state st = P.st;
   if (P.d_state) {
@@ -430,14 +444,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   }
   const int n_pages = min(max(st.n_pages, 0), P.page_capacity);
   const int tail_len = min(max(st.tail_len, 0), kPage);
-  const int uph = n_pages + (tail_len > 0 ? 1 : 0);
+  const int uph = 2 * n_pages + (tail_len > 0 ? 1 : 0);
   const int VH = P.num_kv_heads * P.nqc;
   const int64_t U = int64_t(VH) * uph;
   if (U == 0) {
     for (int vh = blockIdx.x; vh < VH; vh += gridDim.x) {
       const int kvh = vh / P.nqc, chunk = vh % P.nqc;
       const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
-      for (int h = 0; h < gc; ++h) write_result(P, kvh * P.group + chunk * kMaxHeads + h, tid, -INFINITY, 0.f, 0.f);
+      for (int i = tid; i < gc * kD; i += kThreads)
+        write_result(P, kvh * P.group + chunk * kMaxHeads + i / kD, i % kD, -INFINITY, 0.f, 0.f);
     }
     return;
   }
@@ -448,55 +463,38 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   auto owner = [&](int64_t u) { return int(((u + 1) * C - 1) / U); };
   const int64_t u0 = ubeg(c), u1 = ubeg(c + 1);
 
-  // Code tables: half2 (cos, sin) of the decoder angle code/(2^bits-1)*2pi - pi, in float32
-  // (rfsn_v11/quant/polar/decoder.py:36-56).
-  for (int i = tid; i < 2 * kLutEntries; i += kThreads) {
-    const int bits = (i < kLutEntries) ? P.l1_bits : P.deep_bits;
-    const int code = i & (kLutEntries - 1);
-    const int lm1 = (1 << bits) - 1;
-    uint32_t v = 0;
-    if (code <= lm1) {
-      const float norm = __fdiv_rn(float(code), float(lm1));
-      const float ang = __fsub_rn(__fmul_rn(norm, 6.28318530717958647692f), 3.14159265358979323846f);
-      v = pack_h2(d2f(cos(double(ang))), d2f(sin(double(ang))));
+  {
+    const int n1 = 1 << P.l1_bits, n2 = 1 << P.deep_bits;
+    for (int i = tid; i < n1 + n2; i += kThreads) {
+      const int j = i < n1 ? i : kLutEntries + (i - n1);
+      lut[j] = P.lut[j];
     }
-    lut[i] = v;
   }
   __syncthreads();
 
-  // Segments of this CTA (at most two heads).
+  // Segments of this CTA (at most two heads) and this warp's slice of each.
   const int vh_first = int(u0 / uph), vh_last = int((u1 - 1) / uph);
   const int nseg = vh_last - vh_first + 1;
-  int seg_a[2], seg_n[2];
-  for (int s = 0; s < 2; ++s) {
-    seg_a[s] = seg_n[s] = 0;
-    if (s < nseg) {
-      const int64_t hb = int64_t(vh_first + s) * uph;
-      const int64_t a = max(u0, hb), b = min(u1, hb + uph);
-      seg_a[s] = int(a - hb);
-      seg_n[s] = int(b - a);
+  int wa0 = 0, wn0 = 0, wa1 = 0, wn1 = 0;
+  {
+    const int64_t hb0 = int64_t(vh_first) * uph;
+    const int a0 = int(u0 - hb0), n0 = int(min(u1, hb0 + uph) - u0);
+    wa0 = a0 + (warp * n0) / kWarps;
+    wn0 = a0 + ((warp + 1) * n0) / kWarps - wa0;
+    if (nseg > 1) {
+      const int n1 = int(u1 - (hb0 + uph));
+      wa1 = (warp * n1) / kWarps;
+      wn1 = ((warp + 1) * n1) / kWarps - wa1;
     }
   }
-  // This warp's slice of each segment.
-  int wa[2], wn[2];
-  for (int s = 0; s < 2; ++s) {
-    const int lo = seg_a[s] + (warp * seg_n[s]) / kWarps;
-    const int hi = seg_a[s] + ((warp + 1) * seg_n[s]) / kWarps;
-    wa[s] = lo;
-    wn[s] = hi - lo;
-  }
-  const int total = wn[0] + wn[1];
+  const int total = wn0 + wn1;
   uint8_t* stages = smem + P.smem_stage_off + warp * 2 * P.stage_bytes;
 
-  auto unit_of = [&](int i, int& seg, int& j) {
-    if (i < wn[0]) { seg = 0; j = wa[0] + i; }
-    else { seg = 1; j = wa[1] + i - wn[0]; }
-  };
   auto issue = [&](int i) {
     if (i < total) {
-      int seg, j;
-      unit_of(i, seg, j);
-      if (j < n_pages) issue_page(stages + (i & 1) * P.stage_bytes, P, (vh_first + seg) / P.nqc, j, lane);
+      const bool s1 = i >= wn0;
+      const int j = s1 ? wa1 + (i - wn0) : wa0 + i;
+      if (j < 2 * n_pages) issue_half(stages + (i & 1) * P.stage_bytes, P, (vh_first + (s1 ? 1 : 0)) / P.nqc, j >> 1, j & 1, lane);
     }
     cp_async_commit();
   };
@@ -509,26 +507,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
     const int vh = vh_first + s;
     const int kvh = vh / P.nqc, chunk = vh % P.nqc;
     const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
-    float* rec = merge + (s * kWarps + warp) * kPartialStride;
-    if (wn[s] == 0) {
-      store_empty_partial(rec, gc, lane);
-      continue;
+    const int wn = s ? wn1 : wn0, wa = s ? wa1 : wa0;
+    const int i0 = s ? wn0 : 0;
+    if (wn > 0) {
+      load_q_frags(P, kvh * P.group + chunk * kMaxHeads, gc, lane, qf);
+      acc_reset(A);
     }
-    load_q_frags(P, kvh * P.group + chunk * kMaxHeads, gc, lane, qf);
-    acc_reset(A);
-    const int i0 = (s == 0) ? 0 : wn[0];
-    for (int i = i0; i < i0 + wn[s]; ++i) {
+    for (int i = i0; i < i0 + wn; ++i) {
       if (i + 1 < total) cp_async_wait<1>();
       else cp_async_wait<0>();
       __syncwarp();
-      const int j = wa[s] + (i - i0);
-      if (j < n_pages) {
-        const int64_t abs_page = int64_t(st.first_page) + j;
-        const int64_t valid = int64_t(st.seq_len) - abs_page * kPage;
-        const int vt = int(clamp64(valid, 0, kPage));
+      const int j = wa + (i - i0);
+      if (j < 2 * n_pages) {
+        const int page = j >> 1, half = j & 1;
+        const int64_t pos0 = (int64_t(st.first_page) + page) * kPage + half * kHalf;
+        const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, kHalf));
         float rs = 0.f;
-        if (P.int8_radii) rs = __half2float(P.radii_scales[int64_t(kvh) * P.page_capacity + j]);
-        process_page<kFast>(A, stages + (i & 1) * P.stage_bytes, P, lut, qf, rs, vt, lane);
+        if (P.int8_radii) rs = __half2float(P.radii_scales[int64_t(kvh) * P.page_capacity + page]);
+        process_half<kFast>(A, stages + (i & 1) * P.stage_bytes, P, lut, qf, rs, vt, lane);
       } else {
         const int64_t pos0 = (int64_t(st.first_page) + n_pages) * kPage;
         const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, tail_len));
@@ -537,72 +533,148 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
       __syncwarp();
       issue(i + 2);
     }
-    store_warp_partial(A, rec, gc, lane);
+    // Segment 0 partials live in the merge region; segment 1 partials in the warp's own
+    // stage buffers, free once its pipeline has drained.
+    float* rec = s == 0 ? merge + warp * rec_stride : reinterpret_cast<float*>(stages);
+    if (wn > 0) store_warp_partial(A, rec, gc, lane);
+    else store_empty_partial(rec, gc, lane);
   }
   __syncthreads();
 
-  // Merge the warps of each segment; write the result or a CTA partial.
+  // Pass 1: merge the warps of each segment; write the result or this CTA's partial.
   __shared__ int s_last;
+  bool alone_seg[2] = {true, true};
   for (int s = 0; s < nseg; ++s) {
     const int vh = vh_first + s;
     const int kvh = vh / P.nqc, chunk = vh % P.nqc;
     const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
     const int qh0 = kvh * P.group + chunk * kMaxHeads;
-    const int c_lo = owner(int64_t(vh) * uph), c_hi = owner(int64_t(vh) * uph + uph - 1);
-    const bool alone = (c_lo == c_hi);
+    const bool alone = owner(int64_t(vh) * uph) == owner(int64_t(vh) * uph + uph - 1);
+    alone_seg[s] = alone;
     float* slot = P.ws_partials + int64_t(c * 2 + s) * kPartialStride;
-    for (int h = 0; h < gc; ++h) {
-      float M = -INFINITY;
-      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, merge[((s * kWarps + w) * kMaxHeads + h) * TP_PARTIAL_FLOATS]);
+    const float* recs = s == 0 ? merge : reinterpret_cast<const float*>(smem + P.smem_stage_off);
+    const int wstride = s == 0 ? rec_stride : 2 * P.stage_bytes / int(sizeof(float));
+    for (int i = tid; i < gc * kD; i += kThreads) {
+      const int h = i >> 7, d = i & (kD - 1);
+      float m[kWarps];
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) m[w] = recs[w * wstride + h * TP_PARTIAL_FLOATS];
+      float M = m[0];
+#pragma unroll
+      for (int w = 1; w < kWarps; ++w) M = fmaxf(M, m[w]);
       float L = 0.f, O = 0.f;
-      if (M != -INFINITY) {
-        for (int w = 0; w < kWarps; ++w) {
-          const float* r = merge + ((s * kWarps + w) * kMaxHeads + h) * TP_PARTIAL_FLOATS;
-          if (r[0] == -INFINITY) continue;
-          const float f = exp2_approx(r[0] - M);
-          L += r[1] * f;
-          O += r[2 + tid] * f;
-        }
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float* r = recs + w * wstride + h * TP_PARTIAL_FLOATS;
+        const float f = (m[w] == -INFINITY) ? 0.f : exp2_approx(m[w] - M);
+        L = fmaf(r[1], f, L);
+        O = fmaf(r[2 + d], f, O);
       }
       if (alone) {
-        write_result(P, qh0 + h, tid, M, L, O);
+        write_result(P, qh0 + h, d, M, L, O);
       } else {
-        float* rec = slot + h * TP_PARTIAL_FLOATS;
-        if (tid == 0) { rec[0] = M; rec[1] = L; }
-        rec[2 + tid] = O;
+        float* out = slot + h * TP_PARTIAL_FLOATS;
+        if (d == 0) { out[0] = M; out[1] = L; }
+        out[2 + d] = O;
       }
     }
-    if (alone) continue;
-    __threadfence();
-    __syncthreads();
+  }
+  if (alone_seg[0] && alone_seg[1]) return;
+  __syncthreads();
+
+  // Pass 2: per shared head, one thread publishes this CTA's partial (release: barrier, then a
+  // single fence and atomic) and takes a ticket; the last CTA to arrive stages every
+  // contributor's record in shared memory (concurrent cp.async) and merges them.
+  float* scratch = reinterpret_cast<float*>(smem + P.smem_stage_off);
+  for (int s = 0; s < nseg; ++s) {
+    if (alone_seg[s]) continue;
+    const int vh = vh_first + s;
+    const int kvh = vh / P.nqc, chunk = vh % P.nqc;
+    const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
+    const int qh0 = kvh * P.group + chunk * kMaxHeads;
+    const int c_lo = owner(int64_t(vh) * uph), c_hi = owner(int64_t(vh) * uph + uph - 1);
     if (tid == 0) {
+      __threadfence();
       const int prev = atomicAdd(&P.ws_counters[vh], 1);
       s_last = (prev == c_hi - c_lo);
-      if (s_last) P.ws_counters[vh] = 0;
+      if (s_last) {
+        P.ws_counters[vh] = 0;
+        __threadfence();
+      }
     }
     __syncthreads();
-    if (s_last) {
-      __threadfence();
-      for (int h = 0; h < gc; ++h) {
-        float M = -INFINITY;
-        for (int cc = c_lo; cc <= c_hi; ++cc) {
-          const int sc = vh - int(ubeg(cc) / uph);
-          M = fmaxf(M, __ldcg(P.ws_partials + int64_t(cc * 2 + sc) * kPartialStride + h * TP_PARTIAL_FLOATS));
-        }
-        float L = 0.f, O = 0.f;
-        if (M != -INFINITY) {
-          for (int cc = c_lo; cc <= c_hi; ++cc) {
-            const int sc = vh - int(ubeg(cc) / uph);
-            const float* r = P.ws_partials + int64_t(cc * 2 + sc) * kPartialStride + h * TP_PARTIAL_FLOATS;
-            const float m = __ldcg(r);
-            if (m == -INFINITY) continue;
-            const float f = exp2_approx(m - M);
-            L += __ldcg(r + 1) * f;
-            O += __ldcg(r + 2 + tid) * f;
-          }
-        }
-        write_result(P, qh0 + h, tid, M, L, O);
+    if (!s_last) continue;
+    const int n = c_hi - c_lo + 1;
+    // (m, l) of every contributor, then per-head max, weights and sum.
+    int* soff = reinterpret_cast<int*>(scratch);        // [n] slot offsets (floats)
+    float* mw = scratch + ((n + 3) & ~3);               // [n][kMaxHeads]: m, then weight
+    float* lv = mw + n * kMaxHeads;                     // [n][kMaxHeads]
+    float* Ms = lv + n * kMaxHeads;
+    float* Ls = Ms + kMaxHeads;
+    float* recs = Ls + kMaxHeads;                       // staged records (16-byte aligned)
+    for (int ci = tid; ci < n; ci += kThreads) {
+      const int cc = c_lo + ci;
+      soff[ci] = (cc * 2 + (vh - int(ubeg(cc) / uph))) * kPartialStride;
+    }
+    __syncthreads();
+    for (int i = tid; i < n * gc; i += kThreads) {
+      const int ci = i / gc, h = i - ci * gc;
+      const float* r = P.ws_partials + soff[ci] + h * TP_PARTIAL_FLOATS;
+      mw[ci * kMaxHeads + h] = __ldcg(r);
+      lv[ci * kMaxHeads + h] = __ldcg(r + 1);
+    }
+    __syncthreads();
+    if (warp < gc) {
+      const int h = warp;
+      float M = -INFINITY;
+      for (int ci = lane; ci < n; ci += 32) M = fmaxf(M, mw[ci * kMaxHeads + h]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      float L = 0.f;
+      for (int ci = lane; ci < n; ci += 32) {
+        const float m = mw[ci * kMaxHeads + h];
+        const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - M);
+        mw[ci * kMaxHeads + h] = w;
+        L = fmaf(lv[ci * kMaxHeads + h], w, L);
       }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+      if (lane == 0) { Ms[h] = M; Ls[h] = L; }
+    }
+    // Weighted sum of the outputs, contributor records staged in chunks by concurrent cp.async.
+    const int rec_floats = (gc * TP_PARTIAL_FLOATS + 3) & ~3;
+    const int avail = P.scratch_floats - int(recs - scratch);
+    const int chunk_n = max(1, avail / rec_floats);
+    float acc[kMaxHeads * kD / kThreads];
+#pragma unroll
+    for (int k = 0; k < kMaxHeads * kD / kThreads; ++k) acc[k] = 0.f;
+    for (int c0 = 0; c0 < n; c0 += chunk_n) {
+      const int cn = min(chunk_n, n - c0);
+      __syncthreads();
+      for (int ci = warp; ci < cn; ci += kWarps) {
+        const float* src = P.ws_partials + soff[c0 + ci];
+        for (int e = lane * 4; e < rec_floats; e += 128) cp_async16(recs + ci * rec_floats + e, src + e);
+      }
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < kMaxHeads * kD / kThreads; ++k) {
+        const int i = tid + k * kThreads;
+        if (i < gc * kD) {
+          const int h = i >> 7, d = i & (kD - 1);
+          float o = acc[k];
+#pragma unroll 4
+          for (int ci = 0; ci < cn; ++ci)
+            o = fmaf(mw[(c0 + ci) * kMaxHeads + h], recs[ci * rec_floats + h * TP_PARTIAL_FLOATS + 2 + d], o);
+          acc[k] = o;
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxHeads * kD / kThreads; ++k) {
+      const int i = tid + k * kThreads;
+      if (i < gc * kD) write_result(P, qh0 + (i >> 7), i & (kD - 1), Ms[i >> 7], Ls[i >> 7], acc[k]);
     }
     __syncthreads();
   }
@@ -624,6 +696,22 @@ __global__ void combine_kernel(const float* partials, int n_parts, int num_q_hea
     }
   }
   out[int64_t(h) * kD + d] = __float2half_rn(L > 0.f ? O / L : 0.f);
+}
+
+// half2 (cos, sin) of the decoder angle of every code value, the angle evaluated in float32
+// exactly as rfsn_v11/quant/polar/decoder.py:36-56 does (code / (2^bits - 1) * 2pi - pi, each
+// op rounded to float32; the double evaluation below rounds to the same floats), cos and sin
+// correctly rounded to float32, then to float16.
+static void code_table(int bits, uint32_t* out) {
+  const int lm1 = (1 << bits) - 1;
+  for (int code = 0; code <= lm1; ++code) {
+    const float norm = float(double(code) / double(lm1));
+    const float prod = float(double(norm) * double(6.28318530717958647692f));
+    const float ang = float(double(prod) - double(3.14159265358979323846f));
+    const __half c = __float2half_rn(float(cos(double(ang))));
+    const __half s = __float2half_rn(float(sin(double(ang))));
+    out[code] = uint32_t(__half_as_ushort(c)) | (uint32_t(__half_as_ushort(s)) << 16);
+  }
 }
 
 static int g_num_sms = 0;
@@ -716,41 +804,52 @@ int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state 
   P.num_kv_heads = hkv;
   P.group = num_q_heads / hkv;
   P.nqc = (P.group + kMaxHeads - 1) / kMaxHeads;
+  P.gmax = P.group < kMaxHeads ? P.group : kMaxHeads;
   P.scale_log2 = scale * 1.4426950408889634f;
+  for (int i = 0; i < 2 * kLutEntries; ++i) P.lut[i] = 0u;
+  code_table(P.l1_bits, P.lut);
+  code_table(P.deep_bits, P.lut + kLutEntries);
   P.out = static_cast<__half*>(out);
   P.partial_out = partial_out;
   const int grid = grid_size(hkv, num_q_heads);
   P.ws_partials = static_cast<float*>(workspace);
   size_t part_bytes = (size_t(grid) * 2 * kPartialStride * sizeof(float) + 255) & ~size_t(255);
   P.ws_counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + part_bytes);
-  // Stage layout: radii | v codes | level-1 codes | 64-byte bank shift | deep codes | v scales.
+  // Half-page stage: radii | v codes | level-1 codes | 64-byte bank shift | deep codes | v scales.
   auto up = [](int x, int a) { return (x + a - 1) / a * a; };
-  P.off_vcodes = P.radii_page;
-  P.off_l1 = P.off_vcodes + int(kVCodesPage);
-  P.off_deep = P.off_l1 + up(P.l1_page, 128) + 64;
-  P.off_vscales = up(P.off_deep + P.deep_page, 128);
-  P.stage_bytes = up(P.off_vscales + int(kVScalesPage), 128);
+  P.off_vcodes = kHalf * P.radii_row;
+  P.off_l1 = P.off_vcodes + kHalf * kD;
+  P.off_deep = P.off_l1 + up(kHalf * P.l1_row, 128) + 64;
+  P.off_vscales = up(P.off_deep + kHalf * P.deep_row, 128);
+  P.stage_bytes = up(P.off_vscales + kHalf * 8, 128);
+  const int merge_bytes = kWarps * P.gmax * TP_PARTIAL_FLOATS * int(sizeof(float));
   P.smem_merge_off = 2 * kLutEntries * 4;
-  P.smem_stage_off = P.smem_merge_off + 2 * kWarps * kPartialStride * int(sizeof(float));
-  const int smem = P.smem_stage_off + kWarps * 2 * P.stage_bytes;
+  P.smem_stage_off = up(P.smem_merge_off + merge_bytes, 128);
+  // The cross-CTA merge reuses the stage region: per contributor 2*kMaxHeads floats plus a slot
+  // offset, and room for at least one staged record.
+  const int max_contrib = grid + 2;
+  const int scratch_bytes = (max_contrib * (2 * kMaxHeads + 1) + 2 * kMaxHeads + 8 + kPartialStride) * 4;
+  const int stage_region = max(kWarps * 2 * P.stage_bytes, scratch_bytes);
+  P.scratch_floats = stage_region / 4;
+  const int smem = P.smem_stage_off + stage_region;
 
   const bool fast = P.l1_bits == 4 && P.deep_bits == 4 && pool->fmt.split_dim == 64 && !P.int8_radii;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (fast) {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(decode_attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-      attr = true;
-    }
-    decode_attention_kernel<true><<<grid, kThreads, smem, s>>>(P);
-  } else {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(decode_attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-      attr = true;
-    }
-    decode_attention_kernel<false><<<grid, kThreads, smem, s>>>(P);
+  const void* fn = fast ? reinterpret_cast<const void*>(decode_attention_kernel<true>)
+                        : reinterpret_cast<const void*>(decode_attention_kernel<false>);
+  static int attr_bytes[2] = {0, 0};
+  int& have = attr_bytes[fast ? 1 : 0];
+  if (smem > have) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess)
+      return fail(TP_ERR_CUDA, std::string("tp_decode_attention: cannot reserve ") + std::to_string(smem) +
+                                   " bytes of shared memory: " + cudaGetErrorString(e));
+    have = smem;
   }
+  if (fast)
+    decode_attention_kernel<true><<<grid, kThreads, smem, s>>>(P);
+  else
+    decode_attention_kernel<false><<<grid, kThreads, smem, s>>>(P);
   return check_launch("tp_decode_attention");
 }
 

@@ -1,0 +1,96 @@
+"""Time the decode-attention kernel on synthetic layers (also the small case for ncu captures).
+
+    python -m turbopolar_b200.profile_attention --ctx 32768 --hq 32 --hkv 8
+
+Builds enough independent layers that their pages exceed 4x the 126 MB L2 (so every launch
+reads cold data), captures one launch per layer in a CUDA graph and replays it; the per-launch
+device time comes from CUDA events around the replays on the launching stream.  Prints the
+time and the achieved GB/s of algorithmic bytes (compressed pages + dense tail + q + out).
+``--launches N`` instead issues N plain launches over the layers (for ncu: one kernel per
+launch, no graph).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import numpy as np
+import torch
+
+from . import TurboPolarConfig, TurboPolarKVCacheRuntime, build
+from .pages import page_bytes
+
+FORMATS = {
+    "default": {},
+    "adapter": dict(use_int8_radii=True, k_angle_bits_deep=8, split_dim=0),
+}
+L2_BYTES = 126 * 2 ** 20
+
+
+def make_layers(a, dev):
+    cfg = TurboPolarConfig(num_q_heads=a.hq, num_kv_heads=a.hkv, **FORMATS[a.format])
+    per_layer = (a.ctx // 64) * a.hkv * page_bytes(cfg.format_fields())
+    n = a.layers or max(1, math.ceil(4 * L2_BYTES / max(per_layer, 1)))
+    gen = torch.Generator(device=dev)
+    chan = torch.from_numpy(np.random.default_rng(1).uniform(0.5, 4.0, size=128).astype(np.float32)).to(dev)
+    layers = []
+    for i in range(n):
+        gen.manual_seed(a.seed + i)
+        k = (torch.randn((1, a.hkv, a.ctx, 128), generator=gen, device=dev) * chan).half()
+        v = torch.randn((1, a.hkv, a.ctx, 128), generator=gen, device=dev).half()
+        rt = TurboPolarKVCacheRuntime(cfg, max_seq_len=a.ctx, check_finite=False)
+        rt.append(k, v)
+        del k, v
+        layers.append(rt)
+    q = torch.randn((1, a.hq, 128), generator=gen, device=dev).half()
+    return cfg, layers, q
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ctx", type=int, default=32768)
+    ap.add_argument("--hq", type=int, default=32)
+    ap.add_argument("--hkv", type=int, default=8)
+    ap.add_argument("--layers", type=int, default=0, help="0: enough layers to exceed 4x L2")
+    ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--launches", type=int, default=0, help="plain launches instead of graph replays")
+    ap.add_argument("--format", default="default", choices=sorted(FORMATS))
+    ap.add_argument("--seed", type=int, default=0)
+    a = ap.parse_args(argv)
+    build.build()
+    dev = torch.device("cuda:0")
+    cfg, layers, q = make_layers(a, dev)
+    outs = [torch.empty((1, a.hq, 128), dtype=torch.float16, device=dev) for _ in layers]
+    for rt, o in zip(layers, outs):
+        rt.attention(q, out=o)
+    torch.cuda.synchronize()
+    rt0 = layers[0]
+    nbytes = rt0.n_pages * a.hkv * page_bytes(rt0.fmt) + rt0.tail_len * a.hkv * 128 * 4 + a.hq * 128 * 4
+    if a.launches:
+        for i in range(a.launches):
+            layers[i % len(layers)].attention(q, out=outs[i % len(layers)])
+        torch.cuda.synchronize()
+        print(json.dumps({"plain_launches": a.launches}))
+        return
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for rt, o in zip(layers, outs):
+            rt.attention(q, out=o)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(a.reps):
+        g.replay()
+    e.record()
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) * 1e3 / (a.reps * len(layers))
+    print(json.dumps({"ctx": a.ctx, "hq": a.hq, "hkv": a.hkv, "format": a.format, "layers": len(layers),
+                      "us_per_launch": us, "bytes_per_launch": nbytes, "gbs": nbytes / us / 1e3}))
+
+
+if __name__ == "__main__":
+    main()
