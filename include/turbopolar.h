@@ -51,15 +51,18 @@ typedef struct tp_format {
   int32_t int8_radii; /* 0: float16 radii; 1: log-int8 radii + one float16 scale per page */
 } tp_format;
 
-/* Device page pool: one structure-of-arrays store per field, pages of one KV head
- * contiguous, in the reference's block-storage shapes without the batch axis
- * (rfsn_v11/generation/storage.py:17-169, views at :89-102 and :160-169):
- *   radii            [H_kv][page_capacity][64][64]  float16 (int8 when fmt.int8_radii)
+/* Device page pool: one structure-of-arrays store per field, pages of one KV head contiguous,
+ * with the reference's block-storage field sizes (rfsn_v11/generation/storage.py:17-169) and
+ * its codes bit for bit, ordered inside each page for the decode kernel:
+ *   radii            [H_kv][page_capacity][64][64]  float16 (int8 when fmt.int8_radii); float16
+ *                    rows are XOR-swizzled: 16-byte chunk c of row l is stored at chunk c^(l&7)
  *   radii_scales     [H_kv][page_capacity]          float16 (fmt.int8_radii only, else NULL)
- *   angle_codes_l1   [H_kv][page_capacity][64][l1_row_bytes]   uint8, packed
- *   angle_codes_deep [H_kv][page_capacity][64][deep_row_bytes] uint8, packed
- *   v_codes          [H_kv][page_capacity][64][128] int8
- *   v_scales         [H_kv][page_capacity][64][4]   float16
+ *   angle_codes_l1   [H_kv][page_capacity][64][l1_row_bytes]   uint8, packed as the reference
+ *   angle_codes_deep [H_kv][page_capacity][64][deep_row_bytes] uint8, packed as the reference
+ *   v_codes          [H_kv][page_capacity][8192]    uint8 (code ^ 0x80) in mma fragment order
+ *   v_scales         [H_kv][page_capacity][256]     float16 in fragment order
+ * tp_export_pages / tp_import_pages convert pages to and from the reference layout
+ * (radii [64][64] row-major, v_codes int8 [64][128], v_scales [64][4]).
  * Row byte counts come from tp_row_bytes().  Base pointers must be 16-byte aligned. */
 typedef struct tp_page_pool {
   void* radii;
@@ -162,6 +165,20 @@ int tp_fused_scores(const tp_page_pool* pool, int32_t n_pages, const void* q, in
  * benchmarks/turbopolar_fast_attention.py:56-86). */
 int tp_decode_pages(const tp_page_pool* pool, int32_t first_page, int32_t n_pages, void* k_out,
                     void* v_out, void* stream);
+
+/* Copy pages [first_page, first_page + n_pages) of `pool` into pages [0, n_pages) of `ref`,
+ * a pool of the same heads and format laid out exactly as the reference stores blocks
+ * (storage.py:89-102 and :160-169: radii [64][64], v_codes int8 [64][128], v_scales [64][4]),
+ * e.g. to serve TurboPolarKVCacheRuntime.get_fused_attention_inputs
+ * (rfsn_v11/generation/turbo_polar_cache.py:163-198). */
+int tp_export_pages(const tp_page_pool* pool, int32_t first_page, int32_t n_pages, const tp_page_pool* ref,
+                    void* stream);
+
+/* The inverse: load reference-layout pages [0, n_pages) of `ref` into pool pages
+ * [first_page, first_page + n_pages) (payloads handed to the bridge's execute_* calls,
+ * rfsn_v11/kernels/turbo_polar/metal.py:651-792). */
+int tp_import_pages(const tp_page_pool* pool, int32_t first_page, int32_t n_pages, const tp_page_pool* ref,
+                    void* stream);
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* tp_last_error(void);

@@ -21,7 +21,7 @@ STATE_WORDS = 6
 EXPORTED = (
     "tp_row_bytes", "tp_encode_pages", "tp_append", "tp_decode_attention_workspace_size",
     "tp_decode_attention", "tp_combine_partials", "tp_fused_scores", "tp_decode_pages",
-    "tp_last_error", "tp_version",
+    "tp_export_pages", "tp_import_pages", "tp_last_error", "tp_version",
 )
 
 
@@ -63,6 +63,8 @@ def _declare(lib):
         "tp_combine_partials": (ctypes.c_int, [P, I32, I32, P, P]),
         "tp_fused_scores": (ctypes.c_int, [ctypes.POINTER(PagePool), I32, P, I32, I32, F, P, P]),
         "tp_decode_pages": (ctypes.c_int, [ctypes.POINTER(PagePool), I32, I32, P, P, P]),
+        "tp_export_pages": (ctypes.c_int, [ctypes.POINTER(PagePool), I32, I32, ctypes.POINTER(PagePool), P]),
+        "tp_import_pages": (ctypes.c_int, [ctypes.POINTER(PagePool), I32, I32, ctypes.POINTER(PagePool), P]),
         "tp_last_error": (ctypes.c_char_p, []),
         "tp_version": (ctypes.c_int, []),
     }

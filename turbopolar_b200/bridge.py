@@ -16,7 +16,7 @@ from typing import Any, Dict, Optional, Tuple
 import torch
 
 from . import _lib
-from .codec import _pool_of_block, _stream
+from .codec import pool_of_block, _stream
 from .pages import PAGE
 from .payload import PolarKeyBlock, QuantizedVBlock
 
@@ -59,7 +59,7 @@ class CudaKernelBridge:
     # ------------------------------------------------------------------ scores
     def execute_fused_qk(self, q: torch.Tensor, block: PolarKeyBlock, config) -> torch.Tensor:
         """Scores ``(B, H_q, S*64)`` float16 (``metal.py:494-530``)."""
-        pool, B, H, S = _pool_of_block(block)
+        pool, B, H, S = pool_of_block(block)
         q = q.contiguous()
         Hq = q.shape[1]
         out = torch.empty((B, Hq, S * PAGE), dtype=torch.float16, device=q.device)
@@ -71,7 +71,7 @@ class CudaKernelBridge:
     def _attention(self, q, block: Optional[PolarKeyBlock], quant_v: Optional[QuantizedVBlock], tail_k, tail_v,
                    config, actual_seq_len: int) -> torch.Tensor:
         if block is not None:
-            pool, B, H, S = _pool_of_block(block, quant_v)
+            pool, B, H, S = pool_of_block(block, quant_v)
         else:
             pool, B, H, S = None, tail_k.shape[0], tail_k.shape[1], 0
         q = q.contiguous()

@@ -288,17 +288,18 @@ class TurboPolarKVCacheRuntime:
 
     # ------------------------------------------------------------------ reference views
     def _views(self, n: int):
+        """Reference-layout copies of pages [0, n) (``storage.py:89-102, :160-169``)."""
         B, H = self._batch_size, self._num_kv_heads
-        p = self.pool
+        ref = self.pool.export(0, n)
         k = PolarKeyBlock(
-            radii=p.radii[:, :n].view(B, H, n, PAGE, 64),
-            angle_codes_l1=p.angle_codes_l1[:, :n].view(B, H, n, PAGE, p.l1_row),
-            angle_codes_deep=p.angle_codes_deep[:, :n].view(B, H, n, PAGE, p.deep_row),
-            radii_scales=p.radii_scales[:, :n].reshape(B, H, n, 1, 1) if p.radii_scales is not None else None,
+            radii=ref.radii.view(B, H, n, PAGE, 64),
+            angle_codes_l1=ref.angle_codes_l1.view(B, H, n, PAGE, ref.l1_row),
+            angle_codes_deep=ref.angle_codes_deep.view(B, H, n, PAGE, ref.deep_row),
+            radii_scales=ref.radii_scales.view(B, H, n, 1, 1) if ref.radii_scales is not None else None,
             shape=(B, H, n * PAGE, self._head_dim), block_size=PAGE, head_dim=self._head_dim,
             metadata=block_metadata(self.fmt))
-        v = QuantizedVBlock(codes=p.v_codes[:, :n].view(B, H, n, PAGE, 128),
-                            scales=p.v_scales[:, :n].view(B, H, n, PAGE, 4), group_size=32)
+        v = QuantizedVBlock(codes=ref.v_codes.view(B, H, n, PAGE, 128), scales=ref.v_scales.view(B, H, n, PAGE, 4),
+                            group_size=32)
         return k, v
 
     def _tail_views(self):
@@ -317,7 +318,8 @@ class TurboPolarKVCacheRuntime:
 
     def get_fused_attention_inputs(self) -> Tuple[Optional[PolarKeyBlock], Optional[QuantizedVBlock],
                                                   Optional[torch.Tensor], Optional[torch.Tensor], None, int]:
-        """Views for fused attention without re-encoding the tail (``turbo_polar_cache.py:163-198``)."""
+        """Fused-attention inputs without re-encoding the tail (``turbo_polar_cache.py:163-198``):
+        the stored blocks as reference-layout copies and the tail as views of the live buffer."""
         k = v = None
         if self.n_pages > 0:
             k, v = self._views(self.n_pages)
@@ -343,13 +345,13 @@ class TurboPolarKVCacheRuntime:
         if self.n_pages == 0 and part is None:
             return None, None, None, None, self.actual_seq_len
         B, H = self._batch_size, self._num_kv_heads
-        pools = []
+        refs = []
         if self.n_pages:
-            pools.append((self.pool, self.n_pages))
+            refs.append(self.pool.export(0, self.n_pages))
         if part is not None:
-            pools.append((part, 1))
-        cat = lambda name: torch.cat([getattr(p, name)[:, :n] for p, n in pools], dim=1)
-        n = sum(c for _, c in pools)
+            refs.append(part.export(0, 1))
+        cat = lambda name: torch.cat([getattr(r, name) for r in refs], dim=1)
+        n = sum(r.capacity for r in refs)
         l1, deep = cat("angle_codes_l1"), cat("angle_codes_deep")
         k = PolarKeyBlock(
             radii=cat("radii").view(B, H, n, PAGE, 64),

@@ -4,7 +4,9 @@
 * ``PolarQuantDecoder.decode_block`` -- ``rfsn_v11/quant/polar/decoder.py:7-67``
 * ``GroupedVQuantizer.quantize_block / dequantize_block`` -- ``rfsn_v11/quant/v_quant/encoder.py:16-38``
 
-Blocks are 64 tokens (the supported ``block_size``); tensors must live on a CUDA device.
+Payloads are in the reference's layout (the kernels' own page layout is converted on the
+way in and out); blocks are 64 tokens (the supported ``block_size``); tensors must live on a
+CUDA device.
 """
 
 from __future__ import annotations
@@ -16,6 +18,8 @@ import torch
 from . import _lib
 from .pages import PAGE, PagePool
 from .payload import PolarKeyBlock, QuantizedVBlock, block_metadata, format_of_metadata
+
+_VALUE_ONLY_FMT = dict(l1_bits=4, deep_bits=4, split_dim=64, int8_radii=0)
 
 
 def _dtype_code(t: torch.Tensor) -> int:
@@ -63,16 +67,18 @@ class PolarQuantEncoder:
         pool = PagePool(B * H, 1, self.fmt, k_block.device)
         flat = k_block.reshape(B * H, L, D)
         encode_pages(pool, flat, flat, 1, 0)
+        ref = pool.export(0, 1)
         return PolarKeyBlock(
-            radii=pool.radii.view(B, H, L, 64),
-            angle_codes_l1=pool.angle_codes_l1.view(B, H, L, pool.l1_row),
-            angle_codes_deep=pool.angle_codes_deep.view(B, H, L, pool.deep_row),
+            radii=ref.radii.view(B, H, L, 64),
+            angle_codes_l1=ref.angle_codes_l1.view(B, H, L, ref.l1_row),
+            angle_codes_deep=ref.angle_codes_deep.view(B, H, L, ref.deep_row),
             shape=(B, H, L, D), block_size=L, head_dim=D, metadata=block_metadata(self.fmt),
-            radii_scales=pool.radii_scales.view(B, H, 1, 1) if pool.radii_scales is not None else None)
+            radii_scales=ref.radii_scales.view(B, H, 1, 1) if ref.radii_scales is not None else None)
 
 
-def _pool_of_block(block: PolarKeyBlock, quant_v: QuantizedVBlock | None = None) -> tuple[PagePool, int, int, int]:
-    """View a 4-D or 5-D key payload (and optional values) as a page pool [B*H, S, 64, .]."""
+def pool_of_block(block: PolarKeyBlock, quant_v: QuantizedVBlock | None = None):
+    """A kernel-layout pool ``[B*H, S, ...]`` holding a 4-D or 5-D reference key payload and,
+    when given, its values.  Returns ``(pool, B, H, S)``."""
     radii = block.radii
     five = radii.dim() == 5
     if not five:
@@ -83,19 +89,17 @@ def _pool_of_block(block: PolarKeyBlock, quant_v: QuantizedVBlock | None = None)
     rs = None
     if block.radii_scales is not None:
         rs = ex(block.radii_scales).reshape(B * H, S).contiguous()
-    vc = vs = None
     if quant_v is not None:
         vc = quant_v.codes.reshape(B * H, S, PAGE, -1).contiguous()
         vs = quant_v.scales.reshape(B * H, S, PAGE, -1).contiguous()
     else:
-        # Value fields are required by the C ABI's pool check; a one-page dummy is never read.
         vc = torch.zeros((B * H, S, PAGE, 128), dtype=torch.int8, device=radii.device)
         vs = torch.zeros((B * H, S, PAGE, 4), dtype=torch.float16, device=radii.device)
-    pool = PagePool.from_tensors(
+    ref = PagePool.wrap_reference(
         radii.reshape(B * H, S, PAGE, 64).contiguous(),
         ex(block.angle_codes_l1).reshape(B * H, S, PAGE, -1).contiguous(),
         ex(block.angle_codes_deep).reshape(B * H, S, PAGE, -1).contiguous(), rs, vc, vs, fmt)
-    return pool, B, H, S
+    return PagePool.from_reference(ref), B, H, S
 
 
 class PolarQuantDecoder:
@@ -103,7 +107,7 @@ class PolarQuantDecoder:
         _require_cuda(block.radii)
         if block.radii.dtype == torch.int8 and block.radii_scales is None:
             raise ValueError("int8 radii require radii_scales")
-        pool, B, H, S = _pool_of_block(block)
+        pool, B, H, S = pool_of_block(block)
         k = torch.empty((B * H, S * PAGE, 128), dtype=torch.float16, device=block.radii.device)
         v = torch.empty_like(k)
         _lib.check(_lib.lib().tp_decode_pages(ctypes.byref(pool.struct()), 0, S, k.data_ptr(), v.data_ptr(),
@@ -122,18 +126,19 @@ class GroupedVQuantizer:
         B, H, S, L, D = v_block.shape
         if L != PAGE or D != 128:
             raise NotImplementedError("quantize_block expects (B, H, S, 64, 128) values")
-        pool = PagePool(B * H, S, dict(l1_bits=4, deep_bits=4, split_dim=64, int8_radii=0), v_block.device)
+        pool = PagePool(B * H, S, _VALUE_ONLY_FMT, v_block.device)
         flat = v_block.reshape(B * H, S * L, D)
         encode_pages(pool, flat, flat, S, 0)
-        return QuantizedVBlock(codes=pool.v_codes.view(B, H, S, L, D), scales=pool.v_scales.view(B, H, S, L, 4),
+        ref = pool.export(0, S)
+        return QuantizedVBlock(codes=ref.v_codes.view(B, H, S, L, D), scales=ref.v_scales.view(B, H, S, L, 4),
                                group_size=self.group_size)
 
     def dequantize_block(self, block: QuantizedVBlock) -> torch.Tensor:
         _require_cuda(block.codes)
         B, H, S, L, D = block.codes.shape
-        pool = PagePool.from_tensors(None, None, None, None, block.codes.reshape(B * H, S, L, D).contiguous(),
-                                     block.scales.reshape(B * H, S, L, 4).contiguous(),
-                                     dict(l1_bits=4, deep_bits=4, split_dim=64, int8_radii=0))
+        ref = PagePool.wrap_reference(None, None, None, None, block.codes.reshape(B * H, S, L, D).contiguous(),
+                                      block.scales.reshape(B * H, S, L, 4).contiguous(), _VALUE_ONLY_FMT)
+        pool = PagePool.from_reference(ref)
         out = torch.empty((B * H, S * L, D), dtype=torch.float16, device=block.codes.device)
         _lib.check(_lib.lib().tp_decode_pages(ctypes.byref(pool.struct()), 0, S, None, out.data_ptr(),
                                               _stream(out.device)))

@@ -43,6 +43,7 @@ constexpr int kMaxHeads = 8;  // query heads per unit (N of the mma)
 constexpr int kHalf = 32;     // tokens per unit
 constexpr int kPartialStride = kMaxHeads * TP_PARTIAL_FLOATS;  // floats per workspace slot
 constexpr int kLutEntries = 256;
+constexpr int kMaxContrib = 192;  // CTAs that can share one head (grid <= kMaxContrib)
 
 struct AttnParams {
   const uint8_t* radii;
@@ -66,11 +67,23 @@ struct AttnParams {
   __half* out;
   float* partial_out;
   float* ws_partials;
-  int* ws_counters;
+  int* ws_error;
   int stage_bytes, off_vcodes, off_l1, off_deep, off_vscales;
-  int smem_merge_off, smem_stage_off, scratch_floats;
+  int smem_bar_off, smem_lut_off, smem_merge_off, smem_stage_off;
   uint32_t lut[2 * kLutEntries];  // half2 (cos, sin) per code: level-1 [0, 256), deep [256, 512)
 };
+
+// Work partition: CTA cc of C owns units [floor(cc*U/C), floor((cc+1)*U/C)).  U < 2^31 and
+// C <= 2^16, so every product below is exact in a double and the quotient's rounding error is
+// far below the distance to the next integer; this keeps 64-bit integer division (a long
+// inline instruction sequence) out of the kernel.
+__device__ __forceinline__ int part_begin(int cc, int C, int U) {
+  return int(floor(double(cc) * double(U) / double(C)));
+}
+// The CTA whose range holds unit u.
+__device__ __forceinline__ int part_owner(int u, int C, int U) {
+  return int(floor((double(u + 1) * double(C) - 1.0) / double(U)));
+}
 
 __device__ __forceinline__ int64_t clamp64(int64_t x, int64_t lo, int64_t hi) { return x < lo ? lo : (x > hi ? hi : x); }
 
@@ -244,25 +257,18 @@ __device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, c
   for (int mt = 0; mt < 2; ++mt) {
     const uint32_t b0 = movmatrix_trans(pack_h2(sc[mt][0], sc[mt][1]));
     const uint32_t b1 = movmatrix_trans(pack_h2(sc[mt][2], sc[mt][3]));
-    const int tau0 = 16 * mt + 2 * t;
-    const uint4 S01 = lds128(vscales + tau0 * 8);
-    const uint4 S89 = lds128(vscales + (tau0 + 8) * 8);
+    // (scale[tok][G], scale[tok+1][G]) for this lane's token pairs (2t, 2t+1) and (2t+8, 2t+9).
+    const uint4 S01 = lds128(vscales + mt * 128 + t * 32);
+    const uint4 S89 = lds128(vscales + mt * 128 + t * 32 + 16);
+    const uint32_t s01[4] = {S01.x, S01.y, S01.z, S01.w}, s89[4] = {S89.x, S89.y, S89.z, S89.w};
 #pragma unroll
     for (int G = 0; G < 4; ++G) {
-      const uint32_t sel = (G & 1) ? 0x7632u : 0x5410u;
-      const uint32_t sA = prmt(G < 2 ? S01.x : S01.y, G < 2 ? S01.z : S01.w, sel);
-      const uint32_t sB = prmt(G < 2 ? S89.x : S89.y, G < 2 ? S89.z : S89.w, sel);
-      const uint32_t bg0 = hmul2u(b0, sA), bg1 = hmul2u(b1, sB);
-      const int chunk = 2 * G + (g >> 2), within = 4 * (g & 3);
-      const uint32_t w0 = lds32(vcodes + tau0 * 128 + (((chunk ^ (tau0 & 7))) << 4) + within);
-      const uint32_t w1 = lds32(vcodes + (tau0 + 1) * 128 + (((chunk ^ ((tau0 + 1) & 7))) << 4) + within);
-      const uint32_t w2 = lds32(vcodes + (tau0 + 8) * 128 + (((chunk ^ ((tau0 + 8) & 7))) << 4) + within);
-      const uint32_t w3 = lds32(vcodes + (tau0 + 9) * 128 + (((chunk ^ ((tau0 + 9) & 7))) << 4) + within);
-      const uint32_t xl01 = prmt(w0, w1, 0x5140) ^ 0x80808080u, xh01 = prmt(w0, w1, 0x7362) ^ 0x80808080u;
-      const uint32_t xl23 = prmt(w2, w3, 0x5140) ^ 0x80808080u, xh23 = prmt(w2, w3, 0x7362) ^ 0x80808080u;
+      const uint32_t bg0 = hmul2u(b0, s01[G]), bg1 = hmul2u(b1, s89[G]);
+      // Biased codes of this lane's A fragments for tiles 2G and 2G+1, token pairs interleaved.
+      const uint4 W = lds128(vcodes + mt * 2048 + G * 512 + lane * 16);
       const uint32_t K = 0x64646464u;
-      mma16816(A.o[2 * G], prmt(xl01, K, 0x4140), prmt(xl01, K, 0x4342), prmt(xl23, K, 0x4140), prmt(xl23, K, 0x4342), bg0, bg1);
-      mma16816(A.o[2 * G + 1], prmt(xh01, K, 0x4140), prmt(xh01, K, 0x4342), prmt(xh23, K, 0x4140), prmt(xh23, K, 0x4342), bg0, bg1);
+      mma16816(A.o[2 * G], prmt(W.x, K, 0x4140), prmt(W.x, K, 0x4342), prmt(W.z, K, 0x4140), prmt(W.z, K, 0x4342), bg0, bg1);
+      mma16816(A.o[2 * G + 1], prmt(W.y, K, 0x4140), prmt(W.y, K, 0x4342), prmt(W.w, K, 0x4140), prmt(W.w, K, 0x4342), bg0, bg1);
       mma16816(A.ones[G], kOne, kOne, kOne, kOne, bg0, bg1);
     }
   }
@@ -287,71 +293,97 @@ __device__ __forceinline__ void load_tail_pairs(const void* base, int f32, int64
   }
 }
 
-// The whole dense tail (up to 64 tokens) of KV head kvh, read straight from global memory.
-__device__ void process_tail(WarpAcc& A, const AttnParams& P, int kvh, const uint32_t (&qf)[16], int valid_tokens,
-                             int lane) {
+// The whole dense tail (up to 64 tokens) of KV head kvh, read straight from global memory in
+// two 32-token halves.  Loop-rolled: it runs once per head, and keeping it
+// small keeps the page loop's instruction stream compact.
+__device__ __forceinline__ void process_tail(WarpAcc& A, const AttnParams& P, int kvh, const uint32_t (&qf)[16],
+                                             int valid_tokens, int lane) {
   const int g = lane >> 2, t = lane & 3;
   const int64_t head0 = int64_t(kvh) * kPage * kD;
-  float sc[4][4];
+#pragma unroll 1
+  for (int half = 0; half < 2; ++half) {
+    const int base = half * kHalf;
+    if (base >= valid_tokens) break;
+    float sc[2][4];
+#pragma unroll 1
+    for (int mt = 0; mt < 2; ++mt) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int r0 = base + 16 * mt + g, r1 = r0 + 8;
 #pragma unroll
-  for (int mt = 0; mt < 4; ++mt) {
-    uint32_t k0[16], k1[16];
-    const int r0 = 16 * mt + g, r1 = r0 + 8;
-    load_tail_pairs(P.tail_k, P.tail_f32, head0 + int64_t(r0) * kD, 32 * t, 16, r0 < valid_tokens, k0);
-    load_tail_pairs(P.tail_k, P.tail_f32, head0 + int64_t(r1) * kD, 32 * t, 16, r1 < valid_tokens, k1);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t a[2], b[2];
+        load_tail_pairs(P.tail_k, P.tail_f32, head0 + int64_t(r0) * kD, 32 * t + 4 * ks, 2, r0 < valid_tokens, a);
+        load_tail_pairs(P.tail_k, P.tail_f32, head0 + int64_t(r1) * kD, 32 * t + 4 * ks, 2, r1 < valid_tokens, b);
+        mma16816(acc, a[0], b[0], a[1], b[1], qf[2 * ks], qf[2 * ks + 1]);
+      }
+      const float v0 = r0 < valid_tokens ? 0.f : -INFINITY, v1 = r1 < valid_tokens ? 0.f : -INFINITY;
+      const float s0 = acc[0] + v0, s1 = acc[1] + v0, s2 = acc[2] + v1, s3 = acc[3] + v1;
+      if (mt == 0) { sc[0][0] = s0; sc[0][1] = s1; sc[0][2] = s2; sc[0][3] = s3; }
+      else { sc[1][0] = s0; sc[1][1] = s1; sc[1][2] = s2; sc[1][3] = s3; }
+    }
+    softmax_update<2>(A, sc, P.scale_log2);
+#pragma unroll 1
+    for (int mt = 0; mt < 2; ++mt) {
+      const float q0 = mt ? sc[1][0] : sc[0][0], q1 = mt ? sc[1][1] : sc[0][1];
+      const float q2 = mt ? sc[1][2] : sc[0][2], q3 = mt ? sc[1][3] : sc[0][3];
+      const uint32_t b0 = movmatrix_trans(pack_h2(q0, q1));
+      const uint32_t b1 = movmatrix_trans(pack_h2(q2, q3));
+      const int tau0 = base + 16 * mt + 2 * t;
+#pragma unroll 1
+      for (int G = 0; G < 4; ++G) {
+        uint32_t w[4][2];
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) mma16816(acc, k0[2 * ks], k1[2 * ks], k0[2 * ks + 1], k1[2 * ks + 1], qf[2 * ks], qf[2 * ks + 1]);
-    sc[mt][0] = r0 < valid_tokens ? acc[0] : -INFINITY;
-    sc[mt][1] = r0 < valid_tokens ? acc[1] : -INFINITY;
-    sc[mt][2] = r1 < valid_tokens ? acc[2] : -INFINITY;
-    sc[mt][3] = r1 < valid_tokens ? acc[3] : -INFINITY;
-  }
-  softmax_update<4>(A, sc, P.scale_log2);
+        for (int i = 0; i < 4; ++i) {
+          const int tau = tau0 + (i & 1) + 8 * (i >> 1);
+          load_tail_pairs(P.tail_v, P.tail_f32, head0 + int64_t(tau) * kD, 32 * G + 4 * g, 2, tau < valid_tokens, w[i]);
+        }
+        // w[i][0] = (d0, d1), w[i][1] = (d2, d3) of token tau0 + {0, 1, 8, 9}[i].
+        float d0[4], d1[4];
 #pragma unroll
-  for (int mt = 0; mt < 4; ++mt) {
-    const uint32_t b0 = movmatrix_trans(pack_h2(sc[mt][0], sc[mt][1]));
-    const uint32_t b1 = movmatrix_trans(pack_h2(sc[mt][2], sc[mt][3]));
-    const int tau[4] = {16 * mt + 2 * t, 16 * mt + 2 * t + 1, 16 * mt + 2 * t + 8, 16 * mt + 2 * t + 9};
+        for (int j = 0; j < 4; ++j) { d0[j] = 0.f; d1[j] = 0.f; }
+        mma16816(d0, prmt(w[0][0], w[1][0], 0x5410), prmt(w[0][0], w[1][0], 0x7632),
+                 prmt(w[2][0], w[3][0], 0x5410), prmt(w[2][0], w[3][0], 0x7632), b0, b1);
+        mma16816(d1, prmt(w[0][1], w[1][1], 0x5410), prmt(w[0][1], w[1][1], 0x7632),
+                 prmt(w[2][1], w[3][1], 0x5410), prmt(w[2][1], w[3][1], 0x7632), b0, b1);
+        // Accumulate into tiles 2G and 2G+1 (selects keep the accumulators in registers).
 #pragma unroll
-    for (int G = 0; G < 4; ++G) {
-      uint32_t w[4][2];
+        for (int gg = 0; gg < 4; ++gg) {
+          if (gg == G) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        load_tail_pairs(P.tail_v, P.tail_f32, head0 + int64_t(tau[i]) * kD, 32 * G + 4 * g, 2, tau[i] < valid_tokens, w[i]);
-      // w[i][0] = (d0, d1), w[i][1] = (d2, d3) of token tau[i].
-      mma16816(A.o[2 * G], prmt(w[0][0], w[1][0], 0x5410), prmt(w[0][0], w[1][0], 0x7632),
-               prmt(w[2][0], w[3][0], 0x5410), prmt(w[2][0], w[3][0], 0x7632), b0, b1);
-      mma16816(A.o[2 * G + 1], prmt(w[0][1], w[1][1], 0x5410), prmt(w[0][1], w[1][1], 0x7632),
-               prmt(w[2][1], w[3][1], 0x5410), prmt(w[2][1], w[3][1], 0x7632), b0, b1);
+            for (int j = 0; j < 4; ++j) { A.o[2 * gg][j] += d0[j]; A.o[2 * gg + 1][j] += d1[j]; }
+          }
+        }
+      }
     }
   }
 }
 
 // ----------------------------------------------------------------------------- staging
-// Rows [32*half, 32*half + 32) of page `page` of KV head kvh into a half-page stage.
-__device__ __forceinline__ void issue_half(uint8_t* stage, const AttnParams& P, int kvh, int page, int half, int lane) {
+// Rows [32*half, 32*half + 32) of page `page` of KV head kvh into a half-page stage: one lane
+// issues one bulk copy per field (every field of a half page is contiguous in the pool
+// layout) completing on the stage's mbarrier.
+__device__ __forceinline__ void issue_half(uint8_t* stage, uint64_t* bar, const AttnParams& P, int kvh, int page,
+                                           int half) {
   const int64_t slot = int64_t(kvh) * P.page_capacity + page;
-  const int hr = half * kHalf;
-  const uint8_t* rg = P.radii + slot * P.radii_page + hr * P.radii_row;
-  const int rchunks = (kHalf * P.radii_row) >> 4;
-  if (P.radii_row == 128) {
-#pragma unroll 2
-    for (int i = lane; i < rchunks; i += 32) cp_async16(stage + swz128(i >> 3, i & 7), rg + (i << 4));
-  } else {
-    for (int i = lane; i < rchunks; i += 32) cp_async16(stage + (i << 4), rg + (i << 4));
+  const uint32_t rb = kHalf * P.radii_row, lb = kHalf * P.l1_row, db = kHalf * P.deep_row;
+  fence_proxy_async_smem();
+  mbar_arrive_expect_tx(bar, rb + uint32_t(kHalf * kD) + lb + db + uint32_t(kHalf * 8));
+  bulk_g2s(stage, P.radii + slot * P.radii_page + half * rb, rb, bar);
+  bulk_g2s(stage + P.off_vcodes, reinterpret_cast<const uint8_t*>(P.v_codes) + slot * kVCodesPage + half * (kHalf * kD),
+           kHalf * kD, bar);
+  if (lb) bulk_g2s(stage + P.off_l1, P.l1 + slot * P.l1_page + half * lb, lb, bar);
+  if (db) bulk_g2s(stage + P.off_deep, P.deep + slot * P.deep_page + half * db, db, bar);
+  bulk_g2s(stage + P.off_vscales, reinterpret_cast<const uint8_t*>(P.v_scales) + slot * kVScalesPage + half * (kHalf * 8),
+           kHalf * 8, bar);
+}
+
+// Bounded wait for phase `parity` of a stage barrier (about a second); false on timeout.
+__device__ __forceinline__ bool stage_wait(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > (1ll << 31)) return false;
   }
-  const uint8_t* vg = reinterpret_cast<const uint8_t*>(P.v_codes) + slot * kVCodesPage + hr * kD;
-  uint8_t* vs = stage + P.off_vcodes;
-#pragma unroll
-  for (int i = lane; i < 256; i += 32) cp_async16(vs + swz128(i >> 3, i & 7), vg + (i << 4));
-  const int l1c = (kHalf * P.l1_row) >> 4, dc = (kHalf * P.deep_row) >> 4;
-  const uint8_t* lg = P.l1 + slot * P.l1_page + hr * P.l1_row;
-  for (int i = lane; i < l1c; i += 32) cp_async16(stage + P.off_l1 + (i << 4), lg + (i << 4));
-  const uint8_t* dg = P.deep + slot * P.deep_page + hr * P.deep_row;
-  for (int i = lane; i < dc; i += 32) cp_async16(stage + P.off_deep + (i << 4), dg + (i << 4));
-  const uint8_t* sg = reinterpret_cast<const uint8_t*>(P.v_scales) + slot * kVScalesPage + hr * 8;
-  if (lane < 16) cp_async16(stage + P.off_vscales + (lane << 4), sg + (lane << 4));
+  return true;
 }
 
 __device__ __forceinline__ void load_q_frags(const AttnParams& P, int qh_base, int gc, int lane, uint32_t (&qf)[16]) {
@@ -429,7 +461,7 @@ __device__ __forceinline__ void write_result(const AttnParams& P, int qh, int d,
 template <bool kFast>
 __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __grid_constant__ AttnParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint32_t* lut = reinterpret_cast<uint32_t*>(smem);
+  uint32_t* lut = reinterpret_cast<uint32_t*>(smem + P.smem_lut_off);
   float* merge = reinterpret_cast<float*>(smem + P.smem_merge_off);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gmax = P.gmax;
@@ -446,22 +478,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   const int tail_len = min(max(st.tail_len, 0), kPage);
   const int uph = 2 * n_pages + (tail_len > 0 ? 1 : 0);
   const int VH = P.num_kv_heads * P.nqc;
-  const int64_t U = int64_t(VH) * uph;
-  if (U == 0) {
-    for (int vh = blockIdx.x; vh < VH; vh += gridDim.x) {
-      const int kvh = vh / P.nqc, chunk = vh % P.nqc;
-      const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
-      for (int i = tid; i < gc * kD; i += kThreads)
-        write_result(P, kvh * P.group + chunk * kMaxHeads + i / kD, i % kD, -INFINITY, 0.f, 0.f);
-    }
-    return;
+  const int U = VH * uph;
+  const int C = U < int(gridDim.x) ? U : int(gridDim.x);
+  // Let the split-combine grid become resident now; it waits for this grid to complete.
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  if (blockIdx.x == 0 && tid == 0) {
+    P.ws_error[1] = C;
+    P.ws_error[2] = U;
+    P.ws_error[3] = uph;
   }
-  const int C = int(U < int64_t(gridDim.x) ? U : int64_t(gridDim.x));
+  if (U == 0) return;
   const int c = blockIdx.x;
   if (c >= C) return;
-  auto ubeg = [&](int cc) { return int64_t(cc) * U / C; };
-  auto owner = [&](int64_t u) { return int(((u + 1) * C - 1) / U); };
-  const int64_t u0 = ubeg(c), u1 = ubeg(c + 1);
+  const int u0 = part_begin(c, C, U), u1 = part_begin(c + 1, C, U);
 
   {
     const int n1 = 1 << P.l1_bits, n2 = 1 << P.deep_bits;
@@ -473,16 +502,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   __syncthreads();
 
   // Segments of this CTA (at most two heads) and this warp's slice of each.
-  const int vh_first = int(u0 / uph), vh_last = int((u1 - 1) / uph);
+  const int vh_first = u0 / uph, vh_last = (u1 - 1) / uph;
   const int nseg = vh_last - vh_first + 1;
   int wa0 = 0, wn0 = 0, wa1 = 0, wn1 = 0;
   {
-    const int64_t hb0 = int64_t(vh_first) * uph;
-    const int a0 = int(u0 - hb0), n0 = int(min(u1, hb0 + uph) - u0);
+    const int hb0 = vh_first * uph;
+    const int a0 = u0 - hb0, n0 = min(u1, hb0 + uph) - u0;
     wa0 = a0 + (warp * n0) / kWarps;
     wn0 = a0 + ((warp + 1) * n0) / kWarps - wa0;
     if (nseg > 1) {
-      const int n1 = int(u1 - (hb0 + uph));
+      const int n1 = u1 - (hb0 + uph);
       wa1 = (warp * n1) / kWarps;
       wn1 = ((warp + 1) * n1) / kWarps - wa1;
     }
@@ -490,17 +519,29 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   const int total = wn0 + wn1;
   uint8_t* stages = smem + P.smem_stage_off + warp * 2 * P.stage_bytes;
 
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.smem_bar_off) + warp * 2;
+  if (lane == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  // Lane 0 fills stage i&1 for this warp's unit i: page halves by bulk copy, the dense tail
+  // (read from global memory by process_tail) by a plain arrive so the stage's phase still flips.
   auto issue = [&](int i) {
-    if (i < total) {
+    if (lane == 0 && i < total) {
       const bool s1 = i >= wn0;
       const int j = s1 ? wa1 + (i - wn0) : wa0 + i;
-      if (j < 2 * n_pages) issue_half(stages + (i & 1) * P.stage_bytes, P, (vh_first + (s1 ? 1 : 0)) / P.nqc, j >> 1, j & 1, lane);
+      if (j < 2 * n_pages)
+        issue_half(stages + (i & 1) * P.stage_bytes, &bars[i & 1], P, (vh_first + (s1 ? 1 : 0)) / P.nqc, j >> 1, j & 1);
+      else
+        mbar_arrive(&bars[i & 1]);
     }
-    cp_async_commit();
   };
 
   issue(0);
   issue(1);
+  bool timed_out = false;
   WarpAcc A;
   uint32_t qf[16];
   for (int s = 0; s < nseg; ++s) {
@@ -514,11 +555,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
       acc_reset(A);
     }
     for (int i = i0; i < i0 + wn; ++i) {
-      if (i + 1 < total) cp_async_wait<1>();
-      else cp_async_wait<0>();
-      __syncwarp();
+      const bool ready = stage_wait(&bars[i & 1], (i >> 1) & 1);
+      if (!ready) timed_out = true;
       const int j = wa + (i - i0);
-      if (j < 2 * n_pages) {
+      if (!ready) {
+        // Leave the unit out; the error word tells the host the result is unusable.
+      } else if (j < 2 * n_pages) {
         const int page = j >> 1, half = j & 1;
         const int64_t pos0 = (int64_t(st.first_page) + page) * kPage + half * kHalf;
         const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, kHalf));
@@ -539,21 +581,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
     if (wn > 0) store_warp_partial(A, rec, gc, lane);
     else store_empty_partial(rec, gc, lane);
   }
+  if (timed_out && lane == 0) atomicExch(P.ws_error, 1);  // word 0: 1 after a stage-wait timeout
   __syncthreads();
 
-  // Pass 1: merge the warps of each segment; write the result or this CTA's partial.
-  __shared__ int s_last;
-  bool alone_seg[2] = {true, true};
+  // Merge the warps of each segment and publish this CTA's partial; the split-combine kernel
+  // (launched as a programmatic dependent of this grid) merges the CTAs of every head.
   for (int s = 0; s < nseg; ++s) {
     const int vh = vh_first + s;
-    const int kvh = vh / P.nqc, chunk = vh % P.nqc;
+    const int chunk = vh % P.nqc;
     const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
-    const int qh0 = kvh * P.group + chunk * kMaxHeads;
-    const bool alone = owner(int64_t(vh) * uph) == owner(int64_t(vh) * uph + uph - 1);
-    alone_seg[s] = alone;
     float* slot = P.ws_partials + int64_t(c * 2 + s) * kPartialStride;
     const float* recs = s == 0 ? merge : reinterpret_cast<const float*>(smem + P.smem_stage_off);
     const int wstride = s == 0 ? rec_stride : 2 * P.stage_bytes / int(sizeof(float));
+#pragma unroll 1
     for (int i = tid; i < gc * kD; i += kThreads) {
       const int h = i >> 7, d = i & (kD - 1);
       float m[kWarps];
@@ -570,114 +610,78 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
         L = fmaf(r[1], f, L);
         O = fmaf(r[2 + d], f, O);
       }
-      if (alone) {
-        write_result(P, qh0 + h, d, M, L, O);
-      } else {
-        float* out = slot + h * TP_PARTIAL_FLOATS;
-        if (d == 0) { out[0] = M; out[1] = L; }
-        out[2 + d] = O;
-      }
+      float* out = slot + h * TP_PARTIAL_FLOATS;
+      if (d == 0) { out[0] = M; out[1] = L; }
+      out[2 + d] = O;
     }
   }
-  if (alone_seg[0] && alone_seg[1]) return;
-  __syncthreads();
+}
 
-  // Pass 2: per shared head, one thread publishes this CTA's partial (release: barrier, then a
-  // single fence and atomic) and takes a ticket; the last CTA to arrive stages every
-  // contributor's record in shared memory (concurrent cp.async) and merges them.
-  float* scratch = reinterpret_cast<float*>(smem + P.smem_stage_off);
-  for (int s = 0; s < nseg; ++s) {
-    if (alone_seg[s]) continue;
-    const int vh = vh_first + s;
-    const int kvh = vh / P.nqc, chunk = vh % P.nqc;
-    const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
-    const int qh0 = kvh * P.group + chunk * kMaxHeads;
-    const int c_lo = owner(int64_t(vh) * uph), c_hi = owner(int64_t(vh) * uph + uph - 1);
-    if (tid == 0) {
-      __threadfence();
-      const int prev = atomicAdd(&P.ws_counters[vh], 1);
-      s_last = (prev == c_hi - c_lo);
-      if (s_last) {
-        P.ws_counters[vh] = 0;
-        __threadfence();
-      }
+// Merge the per-CTA partials of one query head -- from the CTAs whose unit ranges cover its
+// (KV head, query chunk) -- and write the output.  One CTA per query head, thread d = channel.
+// Launched as a programmatic dependent of the attention grid: its CTAs become resident while
+// that grid finishes and griddepcontrol.wait releases them once the grid has completed and its
+// memory is visible, so no fence or atomic sits on the path.  Contributor records are staged in
+// shared memory by concurrent 8-byte cp.async copies (one memory round trip per 64 records).
+constexpr int kCombineThreads = kD;
+constexpr int kCombineChunk = 64;
+
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(smem_u32(smem)), "l"(gmem));
+}
+
+__global__ void __launch_bounds__(kCombineThreads) split_combine_kernel(const __grid_constant__ AttnParams P) {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  __shared__ __align__(16) float recs[kCombineChunk][TP_PARTIAL_FLOATS];
+  __shared__ int soff[kMaxContrib];
+  const int tid = threadIdx.x;
+  const int vh = blockIdx.x / P.gmax, h = blockIdx.x % P.gmax;
+  const int kvh = vh / P.nqc, chunk = vh % P.nqc;
+  const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
+  if (h >= gc) return;
+  const int qh = kvh * P.group + chunk * kMaxHeads + h;
+  const int* hdr = P.ws_error + 1;  // [C, U, uph] written by CTA 0 of the attention grid
+  const int C = hdr[0], U = hdr[1], uph = hdr[2];
+  if (U == 0) {
+    write_result(P, qh, tid, -INFINITY, 0.f, 0.f);
+    return;
+  }
+  const int c_lo = part_owner(vh * uph, C, U), c_hi = part_owner(vh * uph + uph - 1, C, U);
+  const int n = c_hi - c_lo + 1;
+  for (int ci = tid; ci < n; ci += kCombineThreads) {
+    const int cc = c_lo + ci;
+    soff[ci] = (cc * 2 + (vh - part_begin(cc, C, U) / uph)) * kPartialStride + h * TP_PARTIAL_FLOATS;
+  }
+  __syncthreads();
+  float M = -INFINITY, L = 0.f, O = 0.f;
+#pragma unroll 1
+  for (int c0 = 0; c0 < n; c0 += kCombineChunk) {
+    const int cn = min(kCombineChunk, n - c0);
+    for (int i = tid; i < cn * (TP_PARTIAL_FLOATS / 2); i += kCombineThreads) {
+      const int ci = i / (TP_PARTIAL_FLOATS / 2), e = 2 * (i - ci * (TP_PARTIAL_FLOATS / 2));
+      cp_async8(&recs[ci][e], P.ws_partials + soff[c0 + ci] + e);
     }
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncthreads();
-    if (!s_last) continue;
-    const int n = c_hi - c_lo + 1;
-    // (m, l) of every contributor, then per-head max, weights and sum.
-    int* soff = reinterpret_cast<int*>(scratch);        // [n] slot offsets (floats)
-    float* mw = scratch + ((n + 3) & ~3);               // [n][kMaxHeads]: m, then weight
-    float* lv = mw + n * kMaxHeads;                     // [n][kMaxHeads]
-    float* Ms = lv + n * kMaxHeads;
-    float* Ls = Ms + kMaxHeads;
-    float* recs = Ls + kMaxHeads;                       // staged records (16-byte aligned)
-    for (int ci = tid; ci < n; ci += kThreads) {
-      const int cc = c_lo + ci;
-      soff[ci] = (cc * 2 + (vh - int(ubeg(cc) / uph))) * kPartialStride;
-    }
-    __syncthreads();
-    for (int i = tid; i < n * gc; i += kThreads) {
-      const int ci = i / gc, h = i - ci * gc;
-      const float* r = P.ws_partials + soff[ci] + h * TP_PARTIAL_FLOATS;
-      mw[ci * kMaxHeads + h] = __ldcg(r);
-      lv[ci * kMaxHeads + h] = __ldcg(r + 1);
-    }
-    __syncthreads();
-    if (warp < gc) {
-      const int h = warp;
-      float M = -INFINITY;
-      for (int ci = lane; ci < n; ci += 32) M = fmaxf(M, mw[ci * kMaxHeads + h]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-      float L = 0.f;
-      for (int ci = lane; ci < n; ci += 32) {
-        const float m = mw[ci * kMaxHeads + h];
-        const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - M);
-        mw[ci * kMaxHeads + h] = w;
-        L = fmaf(lv[ci * kMaxHeads + h], w, L);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-      if (lane == 0) { Ms[h] = M; Ls[h] = L; }
-    }
-    // Weighted sum of the outputs, contributor records staged in chunks by concurrent cp.async.
-    const int rec_floats = (gc * TP_PARTIAL_FLOATS + 3) & ~3;
-    const int avail = P.scratch_floats - int(recs - scratch);
-    const int chunk_n = max(1, avail / rec_floats);
-    float acc[kMaxHeads * kD / kThreads];
-#pragma unroll
-    for (int k = 0; k < kMaxHeads * kD / kThreads; ++k) acc[k] = 0.f;
-    for (int c0 = 0; c0 < n; c0 += chunk_n) {
-      const int cn = min(chunk_n, n - c0);
-      __syncthreads();
-      for (int ci = warp; ci < cn; ci += kWarps) {
-        const float* src = P.ws_partials + soff[c0 + ci];
-        for (int e = lane * 4; e < rec_floats; e += 128) cp_async16(recs + ci * rec_floats + e, src + e);
-      }
-      cp_async_commit();
-      cp_async_wait<0>();
-      __syncthreads();
-#pragma unroll
-      for (int k = 0; k < kMaxHeads * kD / kThreads; ++k) {
-        const int i = tid + k * kThreads;
-        if (i < gc * kD) {
-          const int h = i >> 7, d = i & (kD - 1);
-          float o = acc[k];
+    float Mc = M;
+    for (int ci = 0; ci < cn; ++ci) Mc = fmaxf(Mc, recs[ci][0]);
+    if (Mc != -INFINITY) {
+      const float a = (M == -INFINITY) ? 0.f : exp2_approx(M - Mc);
+      L *= a;
+      O *= a;
 #pragma unroll 4
-          for (int ci = 0; ci < cn; ++ci)
-            o = fmaf(mw[(c0 + ci) * kMaxHeads + h], recs[ci * rec_floats + h * TP_PARTIAL_FLOATS + 2 + d], o);
-          acc[k] = o;
-        }
+      for (int ci = 0; ci < cn; ++ci) {
+        const float m = recs[ci][0];
+        const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - Mc);
+        L = fmaf(recs[ci][1], w, L);
+        O = fmaf(recs[ci][2 + tid], w, O);
       }
-    }
-#pragma unroll
-    for (int k = 0; k < kMaxHeads * kD / kThreads; ++k) {
-      const int i = tid + k * kThreads;
-      if (i < gc * kD) write_result(P, qh0 + (i >> 7), i & (kD - 1), Ms[i >> 7], Ls[i >> 7], acc[k]);
+      M = Mc;
     }
     __syncthreads();
   }
+  write_result(P, qh, tid, M, L, O);
 }
 
 // ----------------------------------------------------------------------------- cross-shard combine
@@ -742,10 +746,7 @@ extern "C" {
 size_t tp_decode_attention_workspace_size(int32_t num_kv_heads, int32_t num_q_heads) {
   if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads) return 0;
   const int grid = grid_size(num_kv_heads, num_q_heads);
-  const int vh = num_kv_heads * ((num_q_heads / num_kv_heads + kMaxHeads - 1) / kMaxHeads);
-  size_t bytes = size_t(grid) * 2 * kPartialStride * sizeof(float);
-  bytes = (bytes + 255) & ~size_t(255);
-  bytes += size_t(vh) * sizeof(int);
+  const size_t bytes = 256 + size_t(grid) * 2 * kPartialStride * sizeof(float);
   return (bytes + 255) & ~size_t(255);
 }
 
@@ -812,9 +813,9 @@ int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state 
   P.out = static_cast<__half*>(out);
   P.partial_out = partial_out;
   const int grid = grid_size(hkv, num_q_heads);
-  P.ws_partials = static_cast<float*>(workspace);
-  size_t part_bytes = (size_t(grid) * 2 * kPartialStride * sizeof(float) + 255) & ~size_t(255);
-  P.ws_counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + part_bytes);
+  if (grid > kMaxContrib) return fail(TP_ERR_UNSUPPORTED, "tp_decode_attention: too many KV heads for one launch");
+  P.ws_error = static_cast<int*>(workspace);  // word 0 error, words 1..3 partition header
+  P.ws_partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
   // Half-page stage: radii | v codes | level-1 codes | 64-byte bank shift | deep codes | v scales.
   auto up = [](int x, int a) { return (x + a - 1) / a * a; };
   P.off_vcodes = kHalf * P.radii_row;
@@ -823,14 +824,11 @@ int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state 
   P.off_vscales = up(P.off_deep + kHalf * P.deep_row, 128);
   P.stage_bytes = up(P.off_vscales + kHalf * 8, 128);
   const int merge_bytes = kWarps * P.gmax * TP_PARTIAL_FLOATS * int(sizeof(float));
-  P.smem_merge_off = 2 * kLutEntries * 4;
+  P.smem_bar_off = 0;                       // 2 stage barriers per warp
+  P.smem_lut_off = 128;
+  P.smem_merge_off = P.smem_lut_off + 2 * kLutEntries * 4;
   P.smem_stage_off = up(P.smem_merge_off + merge_bytes, 128);
-  // The cross-CTA merge reuses the stage region: per contributor 2*kMaxHeads floats plus a slot
-  // offset, and room for at least one staged record.
-  const int max_contrib = grid + 2;
-  const int scratch_bytes = (max_contrib * (2 * kMaxHeads + 1) + 2 * kMaxHeads + 8 + kPartialStride) * 4;
-  const int stage_region = max(kWarps * 2 * P.stage_bytes, scratch_bytes);
-  P.scratch_floats = stage_region / 4;
+  const int stage_region = kWarps * 2 * P.stage_bytes;
   const int smem = P.smem_stage_off + stage_region;
 
   const bool fast = P.l1_bits == 4 && P.deep_bits == 4 && pool->fmt.split_dim == 64 && !P.int8_radii;
@@ -850,7 +848,22 @@ int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state 
     decode_attention_kernel<true><<<grid, kThreads, smem, s>>>(P);
   else
     decode_attention_kernel<false><<<grid, kThreads, smem, s>>>(P);
-  return check_launch("tp_decode_attention");
+  st = check_launch("tp_decode_attention");
+  if (st != TP_OK) return st;
+  // Split combine as a programmatic dependent launch of the attention grid.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(hkv * P.nqc * P.gmax);
+  cfg.blockDim = dim3(kCombineThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, split_combine_kernel, P);
+  if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_decode_attention (combine): ") + cudaGetErrorString(e));
+  return TP_OK;
 }
 
 int tp_combine_partials(const float* partials, int32_t n_parts, int32_t num_q_heads, void* out, void* stream) {

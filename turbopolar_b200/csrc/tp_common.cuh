@@ -34,6 +34,35 @@ constexpr int kPairs = kD / 2;
 constexpr int64_t kVCodesPage = kPage * kD;   // int8 bytes per page per head
 constexpr int64_t kVScalesPage = kPage * 4 * 2;  // fp16 [64][4]
 
+// ----------------------------------------------------------------------------- page layout in HBM
+// The codes are the reference's, bit for bit; their order inside a page is chosen for the
+// decode kernel (tp_export_pages / tp_import_pages convert to and from the reference layout):
+//
+// * float16 radii, row l (token) of 128 bytes: 16-byte chunk c (pairs 8c..8c+7) is stored at
+//   chunk c ^ (l & 7), the XOR swizzle that makes the kernel's row-fragment loads
+//   bank-conflict free once a page is copied linearly into shared memory.  int8 radii rows are
+//   64 bytes and stay linear.
+// * value codes, stored as (code ^ 0x80) -- i.e. code + 128 as a byte -- in mma fragment order:
+//   token l = 16*kk + 8*a + 2*t + b (kk: 16-token step, a: upper/lower 8, t: lane quad column,
+//   b: pair bit) and channel d = 32*G + 4*g + 2*e_hi + e_lo sit at byte
+//   kk*2048 + G*512 + g*64 + t*16 + a*8 + e_hi*4 + e_lo*2 + b,
+//   so lane 4g+t of a warp finds its whole A fragment for group G of step kk in one 16-byte word.
+// * value scales (float16, one per token and 32-channel group) at half index
+//   kk*64 + t*16 + a*8 + G*2 + b, so a lane reads (scale[tok][G], scale[tok+1][G]) pairs for its
+//   two token pairs with two 16-byte loads.
+__host__ __device__ __forceinline__ int radii_f16_offset(int l, int j) {  // bytes
+  return l * 128 + ((((j >> 3) ^ (l & 7))) << 4) + (j & 7) * 2;
+}
+__host__ __device__ __forceinline__ int vcode_offset(int l, int d) {  // bytes
+  const int kk = l >> 4, r = l & 15, a = r >> 3, t = (r >> 1) & 3, b = r & 1;
+  const int G = d >> 5, g = (d >> 2) & 7, e_hi = (d >> 1) & 1, e_lo = d & 1;
+  return kk * 2048 + G * 512 + g * 64 + t * 16 + a * 8 + e_hi * 4 + e_lo * 2 + b;
+}
+__host__ __device__ __forceinline__ int vscale_index(int l, int G) {  // halves
+  const int kk = l >> 4, r = l & 15, a = r >> 3, t = (r >> 1) & 3, b = r & 1;
+  return kk * 64 + t * 16 + a * 8 + G * 2 + b;
+}
+
 // ----------------------------------------------------------------------------- device helpers
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
@@ -76,6 +105,41 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// ----------------------------------------------------------------------------- bulk copies
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+// Make barrier initialisation visible to the async proxy (bulk copies complete on it).
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }
+// Order this thread's earlier generic-proxy shared-memory accesses before later async-proxy ones.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+// One bounded-time probe of phase `parity`; true once that phase has completed.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// 1-D bulk copy global -> shared completing on `bar` (no multicast).  16-byte aligned, size % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 __device__ __forceinline__ float exp2_approx(float x) {

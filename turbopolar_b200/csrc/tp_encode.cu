@@ -201,7 +201,7 @@ template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }
 // owns pairs [16c, 16c+16) and V group c of token l.
 template <typename T>
 __device__ void encode_page(const T* k_rows, const T* v_rows, int64_t row_stride, const PagePtrs& dst,
-                            const PoolArgs& P, uint8_t* s_codes, float* s_red) {
+                            const PoolArgs& P, uint8_t* s_codes, float* s_red, uint8_t* s_v, __half* s_scales) {
   const int tid = threadIdx.x;
   const int l = tid >> 2, c = tid & 3;
   const bool f16_in = sizeof(T) == 2;
@@ -217,9 +217,15 @@ __device__ void encode_page(const T* k_rows, const T* v_rows, int64_t row_stride
     if (P.int8_radii) logr[i] = log_radius(pc.r);
   }
   if (!P.int8_radii) {
-    __half* rr = reinterpret_cast<__half*>(dst.radii) + l * kPairs + 16 * c;
+    // Chunks 2c and 2c+1 of row l, stored at their swizzled positions.
 #pragma unroll
-    for (int i = 0; i < 16; ++i) rr[i] = rad[i];
+    for (int h = 0; h < 2; ++h) {
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        w[i] = uint32_t(__half_as_ushort(rad[8 * h + 2 * i])) | (uint32_t(__half_as_ushort(rad[8 * h + 2 * i + 1])) << 16);
+      *reinterpret_cast<uint4*>(dst.radii + radii_f16_offset(l, 16 * c + 8 * h)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
   } else {
     // encoder.py:38-45: one scale per (head, block) = max|log r| / 127.
     float m = 0.0f;
@@ -254,18 +260,9 @@ __device__ void encode_page(const T* k_rows, const T* v_rows, int64_t row_stride
     }
     const __half sc = v_group_scale(mx, f16_in);
     const float scf = __half2float(sc);
-    uint32_t packed[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      uint32_t w = 0;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) w |= uint32_t(uint8_t(v_code(vals[4 * i + b], scf, f16_in))) << (8 * b);
-      packed[i] = w;
-    }
-    uint4* vd = reinterpret_cast<uint4*>(dst.v_codes + l * kD + 32 * c);
-    vd[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-    vd[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-    dst.v_scales[l * 4 + c] = sc;
+    for (int i = 0; i < 32; ++i) s_v[vcode_offset(l, 32 * c + i)] = uint8_t(v_code(vals[i], scf, f16_in)) ^ 0x80u;
+    s_scales[vscale_index(l, c)] = sc;
   }
   __syncthreads();
   // Pack the angle codes row by row (encoder.py:56-75, :100-130).
@@ -291,6 +288,11 @@ __device__ void encode_page(const T* k_rows, const T* v_rows, int64_t row_stride
     }
     (is_l1 ? dst.l1 : dst.deep)[ii] = out;
   }
+  // Values and scales, staged in the page layout, leave in 16-byte stores.
+  for (int i = tid; i < int(kVCodesPage / 16); i += blockDim.x)
+    reinterpret_cast<uint4*>(dst.v_codes)[i] = reinterpret_cast<const uint4*>(s_v)[i];
+  for (int i = tid; i < int(kVScalesPage / 16); i += blockDim.x)
+    reinterpret_cast<uint4*>(dst.v_scales)[i] = reinterpret_cast<const uint4*>(s_scales)[i];
 }
 
 template <typename T>
@@ -299,10 +301,12 @@ __global__ void __launch_bounds__(256) encode_pages_kernel(PoolArgs P, const T* 
                                                            int n_pages, int32_t* d_state) {
   __shared__ uint8_t s_codes[kPage * kPairs];
   __shared__ float s_red[8];
+  __shared__ __align__(16) uint8_t s_v[kVCodesPage];
+  __shared__ __align__(16) __half s_scales[kPage * 4];
   const int p = blockIdx.x, h = blockIdx.y;
   const int64_t tok0 = src_token0 + int64_t(p) * kPage;
   encode_page<T>(k + h * head_stride + tok0 * token_stride, v + h * head_stride + tok0 * token_stride, token_stride,
-                 P.page(h, dst_page + p), P, s_codes, s_red);
+                 P.page(h, dst_page + p), P, s_codes, s_red, s_v, s_scales);
   if (d_state) {
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -324,6 +328,8 @@ __global__ void __launch_bounds__(256) append_kernel(PoolArgs P, T* tail_k, T* t
                                                      int n_tokens) {
   __shared__ uint8_t s_codes[kPage * kPairs];
   __shared__ float s_red[8];
+  __shared__ __align__(16) uint8_t s_v[kVCodesPage];
+  __shared__ __align__(16) __half s_scales[kPage * 4];
   const int h = blockIdx.x;
   const int n_pages = d_state[0], tail_len = d_state[1];
   const bool overflow = tail_len < 0 || tail_len + n_tokens > kPage;
@@ -343,7 +349,7 @@ __global__ void __launch_bounds__(256) append_kernel(PoolArgs P, T* tail_k, T* t
   }
   __syncthreads();
   if (fills) {
-    encode_page<T>(tk, tv, kD, P.page(h, n_pages), P, s_codes, s_red);
+    encode_page<T>(tk, tv, kD, P.page(h, n_pages), P, s_codes, s_red, s_v, s_scales);
     __syncthreads();
   }
   if (threadIdx.x == 0) {

@@ -72,7 +72,7 @@ __device__ __forceinline__ __half2 decode_pair(const PageView& V, const float2* 
     const float arg = __fmul_rn(float(rc), __half2float(V.radii_scales[slot]));
     r = d2f(exp(double(arg)));
   } else {
-    r = __half2float(reinterpret_cast<const __half*>(V.radii)[(slot * kPage + l) * kPairs + j]);
+    r = __half2float(*reinterpret_cast<const __half*>(V.radii + slot * kPage * 128 + radii_f16_offset(l, j)));
   }
   const float2 cs = t[code];
   return __halves2half2(__float2half_rn(__fmul_rn(r, cs.x)), __float2half_rn(__fmul_rn(r, cs.y)));
@@ -122,10 +122,68 @@ __global__ void decode_pages_kernel(PageView V, int first_page, int n_pages, __h
     __half2* ko = reinterpret_cast<__half2*>(k_out + orow * kD);
     for (int i = 0; i < 16; ++i) ko[16 * c + i] = decode_pair(V, tab, slot, l, 16 * c + i);
   }
-  const int8_t* vc = V.v_codes + (slot * kPage + l) * kD + 32 * c;
-  const float s = __half2float(V.v_scales[(slot * kPage + l) * 4 + c]);
+  const uint8_t* vc = reinterpret_cast<const uint8_t*>(V.v_codes) + slot * kVCodesPage;
+  const float s = __half2float(V.v_scales[slot * kPage * 4 + vscale_index(l, c)]);
   __half* vo = v_out + orow * kD + 32 * c;
-  for (int i = 0; i < 32; ++i) vo[i] = __float2half_rn(__fmul_rn(float(vc[i]), s));
+  for (int i = 0; i < 32; ++i) {
+    const int8_t code = int8_t(vc[vcode_offset(l, 32 * c + i)] ^ 0x80u);
+    vo[i] = __float2half_rn(__fmul_rn(float(code), s));
+  }
+}
+
+// Convert pages between the pool layout and the reference's block-storage layout
+// (rfsn_v11/generation/storage.py:89-102, :160-169): radii rows unswizzled, value codes as
+// plain int8 [token][channel], value scales [token][group].  One CTA per (page, head); thread
+// (token l, quarter c).  to_ref: pool -> ref; otherwise ref -> pool.
+__global__ void convert_pages_kernel(PageView pool, PageView ref, int first_page, bool to_ref, bool keys) {
+  const int p = blockIdx.x, h = blockIdx.y;
+  const int l = threadIdx.x >> 2, c = threadIdx.x & 3;
+  const int64_t ps = int64_t(h) * pool.page_capacity + first_page + p;
+  const int64_t rs = int64_t(h) * ref.page_capacity + p;
+  uint8_t* pr = const_cast<uint8_t*>(pool.radii);
+  uint8_t* rr = const_cast<uint8_t*>(ref.radii);
+  if (!keys) {
+  } else if (pool.int8_radii) {
+    for (int i = 0; i < 16; ++i) {
+      const int64_t po = ps * kPage * 64 + l * 64 + 16 * c + i, ro = rs * kPage * 64 + l * 64 + 16 * c + i;
+      if (to_ref) rr[ro] = pr[po]; else pr[po] = rr[ro];
+    }
+    if (threadIdx.x == 0) {
+      __half* prs = const_cast<__half*>(pool.radii_scales);
+      __half* rrs = const_cast<__half*>(ref.radii_scales);
+      if (to_ref) rrs[rs] = prs[ps]; else prs[ps] = rrs[rs];
+    }
+  } else {
+    for (int i = 0; i < 16; ++i) {
+      const int j = 16 * c + i;
+      __half* a = reinterpret_cast<__half*>(pr + ps * kPage * 128 + radii_f16_offset(l, j));
+      __half* b = reinterpret_cast<__half*>(rr + rs * kPage * 128) + l * kPairs + j;
+      if (to_ref) *b = *a; else *a = *b;
+    }
+  }
+  uint8_t* pl = const_cast<uint8_t*>(pool.l1);
+  uint8_t* rl = const_cast<uint8_t*>(ref.l1);
+  for (int i = c; keys && i < pool.l1_row; i += 4) {
+    const int64_t po = (ps * kPage + l) * pool.l1_row + i, ro = (rs * kPage + l) * pool.l1_row + i;
+    if (to_ref) rl[ro] = pl[po]; else pl[po] = rl[ro];
+  }
+  uint8_t* pd = const_cast<uint8_t*>(pool.deep);
+  uint8_t* rd = const_cast<uint8_t*>(ref.deep);
+  for (int i = c; keys && i < pool.deep_row; i += 4) {
+    const int64_t po = (ps * kPage + l) * pool.deep_row + i, ro = (rs * kPage + l) * pool.deep_row + i;
+    if (to_ref) rd[ro] = pd[po]; else pd[po] = rd[ro];
+  }
+  uint8_t* pv = reinterpret_cast<uint8_t*>(const_cast<int8_t*>(pool.v_codes)) + ps * kVCodesPage;
+  uint8_t* rv = reinterpret_cast<uint8_t*>(const_cast<int8_t*>(ref.v_codes)) + rs * kVCodesPage;
+  for (int i = 0; i < 32; ++i) {
+    const int d = 32 * c + i;
+    if (to_ref) rv[l * kD + d] = pv[vcode_offset(l, d)] ^ 0x80u;
+    else pv[vcode_offset(l, d)] = rv[l * kD + d] ^ 0x80u;
+  }
+  __half* psc = const_cast<__half*>(pool.v_scales) + ps * kPage * 4;
+  __half* rsc = const_cast<__half*>(ref.v_scales) + rs * kPage * 4;
+  if (to_ref) rsc[l * 4 + c] = psc[vscale_index(l, c)];
+  else psc[vscale_index(l, c)] = rsc[l * 4 + c];
 }
 
 }  // namespace tp
@@ -166,6 +224,37 @@ int tp_decode_pages(const tp_page_pool* pool, int32_t first_page, int32_t n_page
                                                                            static_cast<__half*>(k_out),
                                                                            static_cast<__half*>(v_out));
   return check_launch("tp_decode_pages");
+}
+
+static int convert(const tp_page_pool* pool, int32_t first_page, int32_t n_pages, const tp_page_pool* ref,
+                   bool to_ref, void* stream) {
+  Layout L, LR;
+  const bool keys = pool && ref && pool->radii && ref->radii;
+  int st = validate_pool(pool, &L, keys);
+  if (st != TP_OK) return st;
+  st = validate_pool(ref, &LR, keys);
+  if (st != TP_OK) return st;
+  if (pool->num_kv_heads != ref->num_kv_heads || pool->fmt.l1_bits != ref->fmt.l1_bits ||
+      pool->fmt.deep_bits != ref->fmt.deep_bits || pool->fmt.split_dim != ref->fmt.split_dim ||
+      pool->fmt.int8_radii != ref->fmt.int8_radii)
+    return fail(TP_ERR_INVALID, "page conversion: pools differ in heads or format");
+  if (first_page < 0 || n_pages < 0 || int64_t(first_page) + n_pages > pool->page_capacity || n_pages > ref->page_capacity)
+    return fail(TP_ERR_INVALID, "page conversion: page range outside a pool");
+  if (n_pages == 0) return TP_OK;
+  dim3 grid(n_pages, pool->num_kv_heads);
+  convert_pages_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(page_view(*pool, L), page_view(*ref, LR),
+                                                                            first_page, to_ref, keys);
+  return check_launch(to_ref ? "tp_export_pages" : "tp_import_pages");
+}
+
+int tp_export_pages(const tp_page_pool* pool, int32_t first_page, int32_t n_pages, const tp_page_pool* ref,
+                    void* stream) {
+  return convert(pool, first_page, n_pages, ref, true, stream);
+}
+
+int tp_import_pages(const tp_page_pool* pool, int32_t first_page, int32_t n_pages, const tp_page_pool* ref,
+                    void* stream) {
+  return convert(pool, first_page, n_pages, ref, false, stream);
 }
 
 }  // extern "C"
