@@ -274,90 +274,6 @@ __device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, c
   }
 }
 
-// ----------------------------------------------------------------------------- dense tail
-__device__ __forceinline__ void load_tail_pairs(const void* base, int f32, int64_t row_elem, int col0, int n_pairs,
-                                                bool valid, uint32_t* dst) {
-  if (!valid) {
-    for (int i = 0; i < n_pairs; ++i) dst[i] = 0u;
-    return;
-  }
-  if (f32) {
-    const float2* p = reinterpret_cast<const float2*>(static_cast<const float*>(base) + row_elem + col0);
-    for (int i = 0; i < n_pairs; ++i) {
-      const float2 v = p[i];
-      dst[i] = pack_h2(v.x, v.y);
-    }
-  } else {
-    const uint32_t* p = reinterpret_cast<const uint32_t*>(static_cast<const __half*>(base) + row_elem + col0);
-    for (int i = 0; i < n_pairs; ++i) dst[i] = p[i];
-  }
-}
-
-// The whole dense tail (up to 64 tokens) of KV head kvh, read straight from global memory in
-// two 32-token halves.  Loop-rolled: it runs once per head, and keeping it
-// small keeps the page loop's instruction stream compact.
-__device__ __forceinline__ void process_tail(WarpAcc& A, const AttnParams& P, int kvh, const uint32_t (&qf)[16],
-                                             int valid_tokens, int lane) {
-  const int g = lane >> 2, t = lane & 3;
-  const int64_t head0 = int64_t(kvh) * kPage * kD;
-#pragma unroll 1
-  for (int half = 0; half < 2; ++half) {
-    const int base = half * kHalf;
-    if (base >= valid_tokens) break;
-    float sc[2][4];
-#pragma unroll 1
-    for (int mt = 0; mt < 2; ++mt) {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      const int r0 = base + 16 * mt + g, r1 = r0 + 8;
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        uint32_t a[2], b[2];
-        load_tail_pairs(P.tail_k, P.tail_f32, head0 + int64_t(r0) * kD, 32 * t + 4 * ks, 2, r0 < valid_tokens, a);
-        load_tail_pairs(P.tail_k, P.tail_f32, head0 + int64_t(r1) * kD, 32 * t + 4 * ks, 2, r1 < valid_tokens, b);
-        mma16816(acc, a[0], b[0], a[1], b[1], qf[2 * ks], qf[2 * ks + 1]);
-      }
-      const float v0 = r0 < valid_tokens ? 0.f : -INFINITY, v1 = r1 < valid_tokens ? 0.f : -INFINITY;
-      const float s0 = acc[0] + v0, s1 = acc[1] + v0, s2 = acc[2] + v1, s3 = acc[3] + v1;
-      if (mt == 0) { sc[0][0] = s0; sc[0][1] = s1; sc[0][2] = s2; sc[0][3] = s3; }
-      else { sc[1][0] = s0; sc[1][1] = s1; sc[1][2] = s2; sc[1][3] = s3; }
-    }
-    softmax_update<2>(A, sc, P.scale_log2);
-#pragma unroll 1
-    for (int mt = 0; mt < 2; ++mt) {
-      const float q0 = mt ? sc[1][0] : sc[0][0], q1 = mt ? sc[1][1] : sc[0][1];
-      const float q2 = mt ? sc[1][2] : sc[0][2], q3 = mt ? sc[1][3] : sc[0][3];
-      const uint32_t b0 = movmatrix_trans(pack_h2(q0, q1));
-      const uint32_t b1 = movmatrix_trans(pack_h2(q2, q3));
-      const int tau0 = base + 16 * mt + 2 * t;
-#pragma unroll 1
-      for (int G = 0; G < 4; ++G) {
-        uint32_t w[4][2];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int tau = tau0 + (i & 1) + 8 * (i >> 1);
-          load_tail_pairs(P.tail_v, P.tail_f32, head0 + int64_t(tau) * kD, 32 * G + 4 * g, 2, tau < valid_tokens, w[i]);
-        }
-        // w[i][0] = (d0, d1), w[i][1] = (d2, d3) of token tau0 + {0, 1, 8, 9}[i].
-        float d0[4], d1[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) { d0[j] = 0.f; d1[j] = 0.f; }
-        mma16816(d0, prmt(w[0][0], w[1][0], 0x5410), prmt(w[0][0], w[1][0], 0x7632),
-                 prmt(w[2][0], w[3][0], 0x5410), prmt(w[2][0], w[3][0], 0x7632), b0, b1);
-        mma16816(d1, prmt(w[0][1], w[1][1], 0x5410), prmt(w[0][1], w[1][1], 0x7632),
-                 prmt(w[2][1], w[3][1], 0x5410), prmt(w[2][1], w[3][1], 0x7632), b0, b1);
-        // Accumulate into tiles 2G and 2G+1 (selects keep the accumulators in registers).
-#pragma unroll
-        for (int gg = 0; gg < 4; ++gg) {
-          if (gg == G) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) { A.o[2 * gg][j] += d0[j]; A.o[2 * gg + 1][j] += d1[j]; }
-          }
-        }
-      }
-    }
-  }
-}
-
 // ----------------------------------------------------------------------------- staging
 // Rows [32*half, 32*half + 32) of page `page` of KV head kvh into a half-page stage: one lane
 // issues one bulk copy per field (every field of a half page is contiguous in the pool
@@ -476,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   }
   const int n_pages = min(max(st.n_pages, 0), P.page_capacity);
   const int tail_len = min(max(st.tail_len, 0), kPage);
-  const int uph = 2 * n_pages + (tail_len > 0 ? 1 : 0);
+  const int uph = 2 * n_pages;  // the dense tail is handled by split_combine_kernel
   const int VH = P.num_kv_heads * P.nqc;
   const int U = VH * uph;
   const int C = U < int(gridDim.x) ? U : int(gridDim.x);
@@ -526,16 +442,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
     fence_mbar_init();
   }
   __syncwarp();
-  // Lane 0 fills stage i&1 for this warp's unit i: page halves by bulk copy, the dense tail
-  // (read from global memory by process_tail) by a plain arrive so the stage's phase still flips.
+  // Lane 0 fills stage i&1 for this warp's unit i (a page half) by bulk copy.
   auto issue = [&](int i) {
     if (lane == 0 && i < total) {
       const bool s1 = i >= wn0;
       const int j = s1 ? wa1 + (i - wn0) : wa0 + i;
-      if (j < 2 * n_pages)
-        issue_half(stages + (i & 1) * P.stage_bytes, &bars[i & 1], P, (vh_first + (s1 ? 1 : 0)) / P.nqc, j >> 1, j & 1);
-      else
-        mbar_arrive(&bars[i & 1]);
+      issue_half(stages + (i & 1) * P.stage_bytes, &bars[i & 1], P, (vh_first + (s1 ? 1 : 0)) / P.nqc, j >> 1, j & 1);
     }
   };
 
@@ -560,17 +472,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
       const int j = wa + (i - i0);
       if (!ready) {
         // Leave the unit out; the error word tells the host the result is unusable.
-      } else if (j < 2 * n_pages) {
+      } else {
         const int page = j >> 1, half = j & 1;
         const int64_t pos0 = (int64_t(st.first_page) + page) * kPage + half * kHalf;
         const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, kHalf));
         float rs = 0.f;
         if (P.int8_radii) rs = __half2float(P.radii_scales[int64_t(kvh) * P.page_capacity + page]);
         process_half<kFast>(A, stages + (i & 1) * P.stage_bytes, P, lut, qf, rs, vt, lane);
-      } else {
-        const int64_t pos0 = (int64_t(st.first_page) + n_pages) * kPage;
-        const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, tail_len));
-        process_tail(A, P, kvh, qf, vt, lane);
       }
       __syncwarp();
       issue(i + 2);
@@ -630,56 +538,153 @@ __device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(smem_u32(smem)), "l"(gmem));
 }
 
+// Softmax partial of one query head over the dense tail of its KV head (at most 64 float16 or
+// float32 tokens, the reference's partial block; metal.py:305-321 treats them as plain keys
+// and values).  Warp w owns tokens w, w+4, ..., w+60; lane owns channels 4*lane..4*lane+3.
+// Every load of a warp is issued before any is used (one round trip for K, one for V).
+// Returns (m, l, o[channel tid]) in the base-2 domain; reads only data written before the
+// attention grid started.
+template <typename T>
+__device__ __forceinline__ float4 load4(const void* base, int64_t idx) {
+  if (sizeof(T) == 4) return reinterpret_cast<const float4*>(static_cast<const float*>(base) + idx)[0];
+  const uint2 u = reinterpret_cast<const uint2*>(static_cast<const __half*>(base) + idx)[0];
+  const float2 a = __half22float2(u32_as_h2(u.x)), b = __half22float2(u32_as_h2(u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+template <typename T>
+__device__ void tail_partial(const AttnParams& P, int kvh, int qh, int valid, float* s_sc, float* s_o, float& m_out,
+                             float& l_out, float& o_out) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int kWarpsC = kCombineThreads / 32, kPer = kPage / kWarpsC;
+  const int64_t head0 = int64_t(kvh) * kPage * kD;
+  // Query as the kernels read it: float16 (a float32 query is rounded).
+  const int64_t qi = int64_t(qh) * kD + 4 * lane;
+  float4 q4 = P.q_f32 ? load4<float>(P.q, qi) : load4<__half>(P.q, qi);
+  if (P.q_f32) {
+    q4.x = __half2float(__float2half_rn(q4.x)); q4.y = __half2float(__float2half_rn(q4.y));
+    q4.z = __half2float(__float2half_rn(q4.z)); q4.w = __half2float(__float2half_rn(q4.w));
+  }
+  float4 kv[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int t = warp + kWarpsC * j;
+    kv[j] = t < valid ? load4<T>(P.tail_k, head0 + int64_t(t) * kD + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    float dot = q4.x * kv[j].x + q4.y * kv[j].y + q4.z * kv[j].z + q4.w * kv[j].w;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    const int t = warp + kWarpsC * j;
+    if (lane == 0 && t < valid) s_sc[t] = dot * P.scale_log2;
+  }
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int t = warp + kWarpsC * j;
+    kv[j] = t < valid ? load4<T>(P.tail_v, head0 + int64_t(t) * kD + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __syncthreads();
+  float m = -INFINITY;
+  for (int t = 0; t < valid; ++t) m = fmaxf(m, s_sc[t]);
+  float l = 0.f;
+  float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int t = warp + kWarpsC * j;
+    if (t < valid) {
+      const float p = exp2_approx(s_sc[t] - m);
+      l += p;
+      o4.x = fmaf(p, kv[j].x, o4.x); o4.y = fmaf(p, kv[j].y, o4.y);
+      o4.z = fmaf(p, kv[j].z, o4.z); o4.w = fmaf(p, kv[j].w, o4.w);
+    }
+  }
+  reinterpret_cast<float4*>(s_o + warp * kD)[lane] = o4;
+  if (lane == 0) s_sc[kPage + warp] = l;
+  __syncthreads();
+  float o = 0.f;
+  l = 0.f;
+#pragma unroll
+  for (int w = 0; w < kWarpsC; ++w) {
+    o += s_o[w * kD + tid];
+    l += s_sc[kPage + w];
+  }
+  m_out = m;
+  l_out = l;
+  o_out = o;
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(kCombineThreads) split_combine_kernel(const __grid_constant__ AttnParams P) {
-  asm volatile("griddepcontrol.wait;\n" ::: "memory");
   __shared__ __align__(16) float recs[kCombineChunk][TP_PARTIAL_FLOATS];
   __shared__ int soff[kMaxContrib];
+  __shared__ __align__(16) float s_o[(kCombineThreads / 32) * kD];
+  __shared__ float s_sc[kPage + kCombineThreads / 32];
   const int tid = threadIdx.x;
   const int vh = blockIdx.x / P.gmax, h = blockIdx.x % P.gmax;
   const int kvh = vh / P.nqc, chunk = vh % P.nqc;
   const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
-  if (h >= gc) return;
-  const int qh = kvh * P.group + chunk * kMaxHeads + h;
-  const int* hdr = P.ws_error + 1;  // [C, U, uph] written by CTA 0 of the attention grid
-  const int C = hdr[0], U = hdr[1], uph = hdr[2];
-  if (U == 0) {
-    write_result(P, qh, tid, -INFINITY, 0.f, 0.f);
+  if (h >= gc) {
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
     return;
   }
-  const int c_lo = part_owner(vh * uph, C, U), c_hi = part_owner(vh * uph + uph - 1, C, U);
-  const int n = c_hi - c_lo + 1;
-  for (int ci = tid; ci < n; ci += kCombineThreads) {
-    const int cc = c_lo + ci;
-    soff[ci] = (cc * 2 + (vh - part_begin(cc, C, U) / uph)) * kPartialStride + h * TP_PARTIAL_FLOATS;
+  const int qh = kvh * P.group + chunk * kMaxHeads + h;
+  // The dense tail first, overlapped with the attention grid (its inputs predate that grid).
+  tp_state st = P.st;
+  if (P.d_state) {
+    st.n_pages = P.d_state[0];
+    st.tail_len = P.d_state[1];
+    st.seq_len = P.d_state[2];
+    st.first_page = P.d_state[3];
   }
-  __syncthreads();
+  const int n_pages = min(max(st.n_pages, 0), P.page_capacity);
+  const int tail_len = min(max(st.tail_len, 0), kPage);
+  const int64_t tpos0 = (int64_t(st.first_page) + n_pages) * kPage;
+  const int valid = int(clamp64(int64_t(st.seq_len) - tpos0, 0, tail_len));
   float M = -INFINITY, L = 0.f, O = 0.f;
+  if (valid > 0) {
+    if (P.tail_f32) tail_partial<float>(P, kvh, qh, valid, s_sc, s_o, M, L, O);
+    else tail_partial<__half>(P, kvh, qh, valid, s_sc, s_o, M, L, O);
+  }
+
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  const int* hdr = P.ws_error + 1;  // [C, U, uph] written by CTA 0 of the attention grid
+  const int C = hdr[0], U = hdr[1], uph = hdr[2];
+  if (U > 0) {
+    const int c_lo = part_owner(vh * uph, C, U), c_hi = part_owner(vh * uph + uph - 1, C, U);
+    const int n = c_hi - c_lo + 1;
+    for (int ci = tid; ci < n; ci += kCombineThreads) {
+      const int cc = c_lo + ci;
+      soff[ci] = (cc * 2 + (vh - part_begin(cc, C, U) / uph)) * kPartialStride + h * TP_PARTIAL_FLOATS;
+    }
+    __syncthreads();
 #pragma unroll 1
-  for (int c0 = 0; c0 < n; c0 += kCombineChunk) {
-    const int cn = min(kCombineChunk, n - c0);
-    for (int i = tid; i < cn * (TP_PARTIAL_FLOATS / 2); i += kCombineThreads) {
-      const int ci = i / (TP_PARTIAL_FLOATS / 2), e = 2 * (i - ci * (TP_PARTIAL_FLOATS / 2));
-      cp_async8(&recs[ci][e], P.ws_partials + soff[c0 + ci] + e);
-    }
-    cp_async_commit();
-    cp_async_wait<0>();
-    __syncthreads();
-    float Mc = M;
-    for (int ci = 0; ci < cn; ++ci) Mc = fmaxf(Mc, recs[ci][0]);
-    if (Mc != -INFINITY) {
-      const float a = (M == -INFINITY) ? 0.f : exp2_approx(M - Mc);
-      L *= a;
-      O *= a;
-#pragma unroll 4
-      for (int ci = 0; ci < cn; ++ci) {
-        const float m = recs[ci][0];
-        const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - Mc);
-        L = fmaf(recs[ci][1], w, L);
-        O = fmaf(recs[ci][2 + tid], w, O);
+    for (int c0 = 0; c0 < n; c0 += kCombineChunk) {
+      const int cn = min(kCombineChunk, n - c0);
+      for (int i = tid; i < cn * (TP_PARTIAL_FLOATS / 2); i += kCombineThreads) {
+        const int ci = i / (TP_PARTIAL_FLOATS / 2), e = 2 * (i - ci * (TP_PARTIAL_FLOATS / 2));
+        cp_async8(&recs[ci][e], P.ws_partials + soff[c0 + ci] + e);
       }
-      M = Mc;
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncthreads();
+      float Mc = M;
+      for (int ci = 0; ci < cn; ++ci) Mc = fmaxf(Mc, recs[ci][0]);
+      if (Mc != -INFINITY) {
+        const float a = (M == -INFINITY) ? 0.f : exp2_approx(M - Mc);
+        L *= a;
+        O *= a;
+#pragma unroll 4
+        for (int ci = 0; ci < cn; ++ci) {
+          const float m = recs[ci][0];
+          const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - Mc);
+          L = fmaf(recs[ci][1], w, L);
+          O = fmaf(recs[ci][2 + tid], w, O);
+        }
+        M = Mc;
+      }
+      __syncthreads();
     }
-    __syncthreads();
   }
   write_result(P, qh, tid, M, L, O);
 }
