@@ -145,6 +145,25 @@ int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state 
                         int32_t num_q_heads, float scale, void* out, float* partial_out,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the fixed scratch array behind tp_decode_attention_noalloc (2 MiB per device). */
+#define TP_NOALLOC_WORKSPACE_BYTES (2u * 1024u * 1024u)
+
+/* tp_decode_attention without a caller-provided workspace, for callers that cannot allocate
+ * device memory: a plugin inside a host runtime that owns every allocation, code that runs
+ * while a stream is being captured (cudaMalloc is not permitted there), or a latency-critical
+ * path that must not take the allocator's locks.  No counterpart in the reference (its MLX
+ * bridge allocates through MLX on every call).  Scratch is a fixed TP_NOALLOC_WORKSPACE_BYTES
+ * array in the library's device memory on every GPU that loads the library, kept until the
+ * process exits; layouts needing more (tp_decode_attention_workspace_size) are rejected with
+ * TP_ERR_INVALID.  The first call on a device resolves the array's address with that device
+ * current, so make it before capturing a stream.  Every call on a device shares the one
+ * array: calls whose executions overlap on the GPU (concurrent streams) race and must be
+ * serialised by the caller.  Allocates nothing (no cudaMalloc / cudaFree). */
+int tp_decode_attention_noalloc(const tp_page_pool* pool, const tp_tail* tail, tp_state state,
+                                const int32_t* d_state, const void* q, int32_t q_dtype,
+                                int32_t num_q_heads, float scale, void* out, float* partial_out,
+                                void* stream);
+
 /* Merge n_parts partial records per query head, laid out [n_parts][H_q][TP_PARTIAL_FLOATS]
  * (the all-gathered output of tp_decode_attention on each sequence shard), into fp16
  * out[H_q][128]: M = max m_r, L = sum l_r 2^(m_r - M), O = sum o_r 2^(m_r - M) / L. */

@@ -32,6 +32,7 @@
 // launch.
 #include <cfloat>
 #include <cmath>
+#include <mutex>
 
 #include "tp_common.cuh"
 
@@ -869,6 +870,49 @@ int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state 
   const cudaError_t e = cudaLaunchKernelEx(&cfg, split_combine_kernel, P);
   if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_decode_attention (combine): ") + cudaGetErrorString(e));
   return TP_OK;
+}
+
+// ----------------------------------------------------------------------------- no-allocation variant
+// Scratch for tp_decode_attention_noalloc: a fixed array in this module's device memory,
+// created when the library is loaded on a device and held there until the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_workspace[TP_NOALLOC_WORKSPACE_BYTES];
+
+static std::mutex g_noalloc_mutex;
+static void* g_noalloc_ptr[64] = {};  // device address of the array, per device ordinal
+
+int tp_decode_attention_noalloc(const tp_page_pool* pool, const tp_tail* tail, tp_state state, const int32_t* d_state,
+                                const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
+                                float* partial_out, void* stream) {
+  if (!pool) return fail(TP_ERR_INVALID, "page pool is NULL");
+  const size_t need = tp_decode_attention_workspace_size(pool->num_kv_heads, num_q_heads);
+  if (need == 0) return fail(TP_ERR_INVALID, "num_q_heads must be divisible by num_kv_heads for GQA");
+  if (need > sizeof(g_noalloc_workspace))
+    return fail(TP_ERR_INVALID, "tp_decode_attention_noalloc: this head layout needs " + std::to_string(need) +
+                                    " bytes of scratch, above the fixed " +
+                                    std::to_string(sizeof(g_noalloc_workspace)) + "-byte maximum");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_decode_attention_noalloc: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(TP_ERR_UNSUPPORTED, "tp_decode_attention_noalloc: device ordinal above 63");
+  void* ws = nullptr;
+  {
+    // The host-side name of the array is not a device address; resolve it once per device,
+    // with that device current.
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_workspace);
+      if (e != cudaSuccess)
+        return fail(TP_ERR_CUDA, std::string("tp_decode_attention_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+      g_noalloc_ptr[dev] = p;
+    }
+    ws = g_noalloc_ptr[dev];
+  }
+  // Word 0 of the scratch is the sticky stage-wait error word; start this call from zero.
+  e = cudaMemsetAsync(ws, 0, sizeof(int), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_decode_attention_noalloc: ") + cudaGetErrorString(e));
+  return tp_decode_attention(pool, tail, state, d_state, q, q_dtype, num_q_heads, scale, out, partial_out, ws,
+                             sizeof(g_noalloc_workspace), stream);
 }
 
 int tp_combine_partials(const float* partials, int32_t n_parts, int32_t num_q_heads, void* out, void* stream) {
