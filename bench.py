@@ -232,11 +232,16 @@ def run_gpu(args):
         layers.append(rt)
     torch.cuda.synchronize()
 
+    # Per-step inputs (new K, V and q of every layer) are views of one device buffer and the
+    # outputs of another, so the end-to-end leg moves them with one copy each way per step.
     gen.manual_seed(7)
-    k_in = [torch.randn((1, HKV, 1, D), generator=gen, device=dev).half() for _ in range(LAYERS)]
-    v_in = [torch.randn((1, HKV, 1, D), generator=gen, device=dev).half() for _ in range(LAYERS)]
-    q_in = [torch.randn((1, HQ, D), generator=gen, device=dev).half() for _ in range(LAYERS)]
-    out = [torch.empty((1, HQ, D), dtype=torch.float16, device=dev) for _ in range(LAYERS)]
+    per_layer_in = 2 * HKV * D + HQ * D
+    d_in = torch.randn((LAYERS, per_layer_in), generator=gen, device=dev).half()
+    d_out = torch.empty((LAYERS, 1, HQ, D), dtype=torch.float16, device=dev)
+    k_in = [d_in[i, :HKV * D].view(1, HKV, 1, D) for i in range(LAYERS)]
+    v_in = [d_in[i, HKV * D:2 * HKV * D].view(1, HKV, 1, D) for i in range(LAYERS)]
+    q_in = [d_in[i, 2 * HKV * D:].view(1, HQ, D) for i in range(LAYERS)]
+    out = [d_out[i] for i in range(LAYERS)]
 
     if world == 1:
         step = graph.DecodeStep(None, layers=[(layers[i], k_in[i], v_in[i], q_in[i], out[i]) for i in range(LAYERS)])
@@ -310,24 +315,18 @@ def run_gpu(args):
                 "bytes_per_context_token": HKV * 296 // max(world, 1) if world == 1 else HKV * 296}
         del att_graph
 
-    # ---- e2e: host inputs -> device, graph step, outputs -> host, per step.
-    h_k = [x.cpu().pin_memory() for x in k_in]
-    h_v = [x.cpu().pin_memory() for x in v_in]
-    h_q = [x.cpu().pin_memory() for x in q_in]
-    h_o = [torch.empty((1, HQ, D), dtype=torch.float16).pin_memory() for _ in range(LAYERS)]
+    # ---- e2e: host inputs -> device, graph step, outputs -> host, every step.
+    h_in = d_in.cpu().pin_memory()
+    h_out = torch.empty(d_out.shape, dtype=torch.float16).pin_memory()
     e_steps = max(1, min(args.steps, 32))
     barrier()
     s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_wall = time.perf_counter()
     s3.record()
     for _ in range(e_steps):
-        for i in range(LAYERS):
-            k_in[i].copy_(h_k[i], non_blocking=True)
-            v_in[i].copy_(h_v[i], non_blocking=True)
-            q_in[i].copy_(h_q[i], non_blocking=True)
+        d_in.copy_(h_in, non_blocking=True)
         step.replay()
-        for i in range(LAYERS):
-            h_o[i].copy_(out[i], non_blocking=True)
+        h_out.copy_(d_out, non_blocking=True)
     e3.record()
     barrier()
     e_ms = s3.elapsed_time(e3)
@@ -338,8 +337,8 @@ def run_gpu(args):
     t_wall = time.perf_counter() - t_wall
     e_step_bytes = step_bytes / args.steps
     e2e = {"value": e_step_bytes / (e_ms / e_steps * 1e-3) / 1e9, "unit": "GB/s",
-           "h2d_bytes_per_step": LAYERS * (2 * HKV * D * 2 + HQ * D * 2),
-           "d2h_bytes_per_step": LAYERS * HQ * D * 2, "steps": e_steps,
+           "h2d_bytes_per_step": h_in.numel() * h_in.element_size(),
+           "d2h_bytes_per_step": h_out.numel() * h_out.element_size(), "steps": e_steps,
            "wall_ms_per_step": t_wall * 1e3 / e_steps}
 
     err = sum(rt.read_device_error() for rt in layers)
@@ -359,7 +358,10 @@ def run_gpu(args):
                        "parallelism": f"sequence-shard x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (2.48 GB of pages per step vs 126 MB L2)"},
             "decode_tokens_per_s": 1000.0 / ms_step,
-            "gpu_launches": args.steps * LAYERS * (2 if world == 1 else 3),
+            # Rank 0's kernels per layer: the page pass and the PDL split-combine of
+            # tp_decode_attention, plus tp_append at N=1 (the last rank appends when sharded)
+            # or tp_combine_partials when sharded.
+            "gpu_launches": args.steps * LAYERS * 3,
             "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary(),
             "device_errors": err,
         }

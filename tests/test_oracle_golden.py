@@ -139,3 +139,29 @@ def test_adapter_sequence_oracle(golden):
             tv = model.partial_v[0] if model.partial_v is not None else None
             out = attention.attention_dense_tail(qs[i][0, :, 0, :], pages, fmt, tk, tv, i + 1, 1 / np.sqrt(128))
             assert np.max(np.abs(out - want[i][0].astype(np.float64))) < 3e-3, (name, i)
+
+
+def _oracle_prefill(k, v):
+    """Decompress-on-read of a cache holding ``k, v`` ``(1, H, T, 128)``: full blocks plus the
+    tail zero-padded to a block, each encoded and decoded (``turbo_polar_cache.py:200-319``,
+    ``turbopolar_fast_attention.py:56-86``), cut to T tokens."""
+    fmt = dict(l1_bits=4, deep_bits=8, split_dim=0)
+    T = k.shape[2]
+    n = -(-T // 64)
+    pad = lambda x: np.concatenate([x, np.zeros(x.shape[:2] + (n * 64 - T, 128), x.dtype)], axis=2)
+    kb = pad(k).reshape(1, k.shape[1], n, 64, 128)
+    vb = pad(v).reshape(1, v.shape[1], n, 64, 128)
+    enc = polar.encode_block(kb, int8_radii=True, **fmt)
+    kd = polar.decode_block(enc["radii"], enc["angle_codes_l1"], enc["angle_codes_deep"], enc["radii_scales"], **fmt)
+    codes, scales = vquant.quantize(vb)
+    vd = vquant.dequantize(codes, scales)
+    return kd.reshape(k.shape[:2] + (n * 64, 128))[:, :, :T], vd.reshape(k.shape[:2] + (n * 64, 128))[:, :, :T]
+
+
+def test_prefill_decompress_on_read(golden):
+    """The reference adapter's update_and_fetch on two prefill chunks (100 then 30 tokens)."""
+    kp, vp, kp2, vp2 = inputs.prefill_inputs()
+    k1, v1 = _oracle_prefill(kp, vp)
+    k2, v2 = _oracle_prefill(np.concatenate([kp, kp2], axis=2), np.concatenate([vp, vp2], axis=2))
+    for got, key in ((k1, "k_out"), (v1, "v_out"), (k2, "k_out2"), (v2, "v_out2")):
+        np.testing.assert_array_equal(got.view(np.uint16), golden[f"prefill/{key}"].view(np.uint16))
