@@ -337,3 +337,25 @@ def test_full_size_c3_layer_vs_oracle():
     out = N(rt.attention(T(q)))[0].astype(np.float64)
     want = oracle_attention(q[0], k, v, fmt_of(cfg), False, cfg.attention_scale)
     assert np.max(np.abs(out - want)) < ATOL
+
+
+@pytest.mark.parametrize("tokens", [40, 64, 100, 200])
+def test_decompress_multi_head_vs_oracle(tokens):
+    """Decompress-on-read (stored pages, then the tail zero-padded, encoded and decoded) for
+    several heads, bit-exact against the oracle codec."""
+    from turbopolar_b200 import TurboPolarKVCacheRuntime
+    from oracle import polar, vquant
+    cfg = _cfg(num_q_heads=8, num_kv_heads=4)
+    k, v = kv_inputs(30 + tokens, 4, tokens, np.float16)
+    rt = TurboPolarKVCacheRuntime(cfg)
+    rt.append(T(k), T(v))
+    kd, vd = rt.decompress(padded_tail=True)
+    n = -(-tokens // 64)
+    pad = lambda x: np.concatenate([x, np.zeros(x.shape[:2] + (n * 64 - tokens, 128), x.dtype)], axis=2)
+    kb, vb = pad(k).reshape(1, 4, n, 64, 128), pad(v).reshape(1, 4, n, 64, 128)
+    enc = polar.encode_block(kb)
+    want_k = polar.decode_block(enc["radii"], enc["angle_codes_l1"], enc["angle_codes_deep"], None)
+    codes, scales = vquant.quantize(vb)
+    want_v = vquant.dequantize(codes, scales)
+    np.testing.assert_array_equal(N(kd).view(np.uint16), want_k.reshape(1, 4, n * 64, 128)[:, :, :tokens].view(np.uint16))
+    np.testing.assert_array_equal(N(vd).view(np.uint16), want_v.reshape(1, 4, n * 64, 128)[:, :, :tokens].view(np.uint16))

@@ -370,18 +370,29 @@ class TurboPolarKVCacheRuntime:
         (``benchmarks/turbopolar_fast_attention.py:56-86``)."""
         B, H = self._batch_size, self._num_kv_heads
         part = self._encode_padded_tail() if padded_tail else None
-        n = self.n_pages + (1 if part is not None else 0)
-        k = torch.empty((self.heads, n * PAGE, 128), dtype=torch.float16, device=self.device)
-        v = torch.empty_like(k)
         lib = _lib.lib()
         s = _stream(self.device)
+
+        def decode(pool: PagePool, n: int):
+            # tp_decode_pages writes [heads][n * 64][128].
+            kk = torch.empty((self.heads, n * PAGE, 128), dtype=torch.float16, device=self.device)
+            vv = torch.empty_like(kk)
+            _lib.check(lib.tp_decode_pages(ctypes.byref(pool.struct()), 0, n, kk.data_ptr(), vv.data_ptr(), s))
+            return kk, vv
+
+        parts = []
         if self.n_pages:
-            _lib.check(lib.tp_decode_pages(ctypes.byref(self.pool.struct()), 0, self.n_pages,
-                                           k.data_ptr(), v.data_ptr(), s))
+            parts.append(decode(self.pool, self.n_pages))
         if part is not None:
-            off = self.n_pages * PAGE * 128 * 2
-            _lib.check(lib.tp_decode_pages(ctypes.byref(part.struct()), 0, 1, k.data_ptr() + off,
-                                           v.data_ptr() + off, s))
+            parts.append(decode(part, 1))
+        if not parts:
+            k = torch.empty((self.heads, 0, 128), dtype=torch.float16, device=self.device)
+            v = torch.empty_like(k)
+        elif len(parts) == 1:
+            k, v = parts[0]
+        else:
+            k = torch.cat([p_[0] for p_ in parts], dim=1)
+            v = torch.cat([p_[1] for p_ in parts], dim=1)
         if not padded_tail and self.tail_len:
             k = torch.cat([k, self.tail_k[:, :self.tail_len].to(torch.float16)], dim=1)
             v = torch.cat([v, self.tail_v[:, :self.tail_len].to(torch.float16)], dim=1)

@@ -64,6 +64,7 @@ struct AttnParams {
   const void* q;
   int q_f32;
   int num_q_heads, num_kv_heads, group, nqc, gmax;
+  int main_grid;  // CTAs of the page pass
   float scale_log2;
   __half* out;
   float* partial_out;
@@ -280,18 +281,20 @@ __device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, c
 // issues one bulk copy per field (every field of a half page is contiguous in the pool
 // layout) completing on the stage's mbarrier.
 __device__ __forceinline__ void issue_half(uint8_t* stage, uint64_t* bar, const AttnParams& P, int kvh, int page,
-                                           int half) {
+                                           int half, uint64_t pol) {
   const int64_t slot = int64_t(kvh) * P.page_capacity + page;
   const uint32_t rb = kHalf * P.radii_row, lb = kHalf * P.l1_row, db = kHalf * P.deep_row;
   fence_proxy_async_smem();
   mbar_arrive_expect_tx(bar, rb + uint32_t(kHalf * kD) + lb + db + uint32_t(kHalf * 8));
-  bulk_g2s(stage, P.radii + slot * P.radii_page + half * rb, rb, bar);
-  bulk_g2s(stage + P.off_vcodes, reinterpret_cast<const uint8_t*>(P.v_codes) + slot * kVCodesPage + half * (kHalf * kD),
-           kHalf * kD, bar);
-  if (lb) bulk_g2s(stage + P.off_l1, P.l1 + slot * P.l1_page + half * lb, lb, bar);
-  if (db) bulk_g2s(stage + P.off_deep, P.deep + slot * P.deep_page + half * db, db, bar);
-  bulk_g2s(stage + P.off_vscales, reinterpret_cast<const uint8_t*>(P.v_scales) + slot * kVScalesPage + half * (kHalf * 8),
-           kHalf * 8, bar);
+  bulk_g2s_hint(stage, P.radii + slot * P.radii_page + half * rb, rb, bar, pol);
+  bulk_g2s_hint(stage + P.off_vcodes,
+                reinterpret_cast<const uint8_t*>(P.v_codes) + slot * kVCodesPage + half * (kHalf * kD), kHalf * kD, bar,
+                pol);
+  if (lb) bulk_g2s_hint(stage + P.off_l1, P.l1 + slot * P.l1_page + half * lb, lb, bar, pol);
+  if (db) bulk_g2s_hint(stage + P.off_deep, P.deep + slot * P.deep_page + half * db, db, bar, pol);
+  bulk_g2s_hint(stage + P.off_vscales,
+                reinterpret_cast<const uint8_t*>(P.v_scales) + slot * kVScalesPage + half * (kHalf * 8), kHalf * 8, bar,
+                pol);
 }
 
 // Bounded wait for phase `parity` of a stage barrier (about a second); false on timeout.
@@ -399,24 +402,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   const int C = U < int(gridDim.x) ? U : int(gridDim.x);
   // Let the split-combine grid become resident now; it waits for this grid to complete.
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-  if (blockIdx.x == 0 && tid == 0) {
-    P.ws_error[1] = C;
-    P.ws_error[2] = U;
-    P.ws_error[3] = uph;
-  }
   if (U == 0) return;
   const int c = blockIdx.x;
   if (c >= C) return;
   const int u0 = part_begin(c, C, U), u1 = part_begin(c + 1, C, U);
-
-  {
-    const int n1 = 1 << P.l1_bits, n2 = 1 << P.deep_bits;
-    for (int i = tid; i < n1 + n2; i += kThreads) {
-      const int j = i < n1 ? i : kLutEntries + (i - n1);
-      lut[j] = P.lut[j];
-    }
-  }
-  __syncthreads();
 
   // Segments of this CTA (at most two heads) and this warp's slice of each.
   const int vh_first = u0 / uph, vh_last = (u1 - 1) / uph;
@@ -443,17 +432,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
     fence_mbar_init();
   }
   __syncwarp();
+  const uint64_t pol = l2_evict_first_policy();
   // Lane 0 fills stage i&1 for this warp's unit i (a page half) by bulk copy.
   auto issue = [&](int i) {
     if (lane == 0 && i < total) {
       const bool s1 = i >= wn0;
       const int j = s1 ? wa1 + (i - wn0) : wa0 + i;
-      issue_half(stages + (i & 1) * P.stage_bytes, &bars[i & 1], P, (vh_first + (s1 ? 1 : 0)) / P.nqc, j >> 1, j & 1);
+      issue_half(stages + (i & 1) * P.stage_bytes, &bars[i & 1], P, (vh_first + (s1 ? 1 : 0)) / P.nqc, j >> 1, j & 1,
+                 pol);
     }
   };
 
+  // The first two units of every warp are in flight before anything else runs.
   issue(0);
   issue(1);
+  {
+    const int n1 = 1 << P.l1_bits, n2 = 1 << P.deep_bits;
+    for (int i = tid; i < n1 + n2; i += kThreads) {
+      const int j = i < n1 ? i : kLutEntries + (i - n1);
+      lut[j] = P.lut[j];
+    }
+  }
+  __syncthreads();
   bool timed_out = false;
   WarpAcc A;
   uint32_t qf[16];
@@ -649,8 +649,10 @@ __global__ void __launch_bounds__(kCombineThreads) split_combine_kernel(const __
   }
 
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
-  const int* hdr = P.ws_error + 1;  // [C, U, uph] written by CTA 0 of the attention grid
-  const int C = hdr[0], U = hdr[1], uph = hdr[2];
+  // The page pass's partition, recomputed from the same state it read.
+  const int uph = 2 * n_pages;
+  const int U = P.num_kv_heads * P.nqc * uph;
+  const int C = U < P.main_grid ? U : P.main_grid;
   if (U > 0) {
     const int c_lo = part_owner(vh * uph, C, U), c_hi = part_owner(vh * uph + uph - 1, C, U);
     const int n = c_hi - c_lo + 1;
@@ -819,8 +821,9 @@ int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state 
   P.out = static_cast<__half*>(out);
   P.partial_out = partial_out;
   const int grid = grid_size(hkv, num_q_heads);
+  P.main_grid = grid;
   if (grid > kMaxContrib) return fail(TP_ERR_UNSUPPORTED, "tp_decode_attention: too many KV heads for one launch");
-  P.ws_error = static_cast<int*>(workspace);  // word 0 error, words 1..3 partition header
+  P.ws_error = static_cast<int*>(workspace);  // word 0: error
   P.ws_partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
   // Half-page stage: radii | v codes | level-1 codes | 64-byte bank shift | deep codes | v scales.
   auto up = [](int x, int a) { return (x + a - 1) / a * a; };
@@ -845,6 +848,12 @@ int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state 
   int& have = attr_bytes[fast ? 1 : 0];
   if (smem > have) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    // All of the unified L1/shared array as shared memory, so the split-combine CTAs fit beside
+    // a page-pass CTA and start (and finish the dense tail) while the page pass runs.
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(split_combine_kernel),
+                               cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess)
       return fail(TP_ERR_CUDA, std::string("tp_decode_attention: cannot reserve ") + std::to_string(smem) +
                                    " bytes of shared memory: " + cudaGetErrorString(e));
