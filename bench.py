@@ -4,8 +4,9 @@ Workload (config 3 of the measurement plan): 32 layers, 32 query / 8 KV heads, h
 block 64, batch 1, fp16, default key format (4-bit level-1 and deep angles, split_dim 64,
 float16 radii) and grouped int8 values.  Each layer's cache is prefilled with 32768 synthetic
 tokens (K ~ N(0,1) * c with a fixed per-channel c ~ U(0.5, 4), V ~ N(0,1), seeded), then a
-"step" is one decode step: for every layer, append one token and run fused attention.  The
-step is captured once as a CUDA graph (the cache counters live on the device) and replayed.
+"step" is one decode step: for every layer, append one token and run fused attention (one
+tp_decode_step call per layer).  The step is captured once as a CUDA graph (the cache
+counters live on the device) and replayed.
 
 Reported (one JSON line on rank 0):
   value     -- decode-attention HBM GB/s over the whole job: algorithmic compressed bytes per
@@ -359,9 +360,8 @@ def run_gpu(args):
                        "l2": "inputs larger than L2 (2.48 GB of pages per step vs 126 MB L2)"},
             "decode_tokens_per_s": 1000.0 / ms_step,
             # Rank 0's kernels per layer: the page pass and the PDL split-combine of
-            # tp_decode_attention, plus tp_append at N=1 (the last rank appends when sharded)
-            # or tp_combine_partials when sharded.
-            "gpu_launches": args.steps * LAYERS * 3,
+            # tp_decode_step (N=1) or tp_decode_attention, plus tp_combine_partials when sharded.
+            "gpu_launches": args.steps * LAYERS * (2 if world == 1 else 3),
             "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary(),
             "device_errors": err,
         }

@@ -145,6 +145,20 @@ int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state 
                         int32_t num_q_heads, float scale, void* out, float* partial_out,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* One decode step in one call: append one token per KV head, then attend over everything
+ * including it.  Replaces TurboPolarFastCache.decode_attention
+ * (benchmarks/turbopolar_fast_attention.py:106-188), i.e. TurboPolarKVCacheRuntime.append
+ * (rfsn_v11/generation/turbo_polar_cache.py:106-161) followed by the fused attention above,
+ * with the same results as tp_append + tp_decode_attention.  k_new / v_new hold token rows
+ * [H_kv][128] in kv_dtype (the tail's dtype), heads head_stride elements apart (16-byte
+ * aligned rows).  The state words d_state (required) are read at the start and advanced by
+ * the call on the device; when the token completes the tail's page, the page is encoded into
+ * pool page n_pages first.  A full pool drops the token and sets d_state[4] = 2. */
+int tp_decode_step(const tp_page_pool* pool, const tp_tail* tail, int32_t* d_state,
+                   const void* k_new, const void* v_new, int32_t kv_dtype, int64_t head_stride,
+                   const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
+                   float* partial_out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Size of the fixed scratch array behind tp_decode_attention_noalloc (2 MiB per device). */
 #define TP_NOALLOC_WORKSPACE_BYTES (2u * 1024u * 1024u)
 

@@ -192,8 +192,9 @@ def test_device_state_path_matches_host_state():
 
 
 def test_cuda_graph_decode_steps_match_eager():
-    """Capture append(1 token) + attention once; replay it for many steps (counters advance on
-    the device) and compare with an eager runtime fed the same tokens."""
+    """Capture a decode step (append 1 token + attention, one tp_decode_step) once; replay it
+    for many steps (counters advance on the device) and compare with an eager runtime fed the
+    same tokens through append + attention."""
     from turbopolar_b200 import TurboPolarKVCacheRuntime
     cfg = _cfg(num_q_heads=8, num_kv_heads=2)
     k, v = kv_inputs(21, 2, 60 + 80, np.float16)
@@ -213,7 +214,13 @@ def test_cuda_graph_decode_steps_match_eager():
         vin.copy_(T(v[:, :, i:i + 1]))
         step.replay()
         e_rt.append(T(k[:, :, i:i + 1]), T(v[:, :, i:i + 1]))
-        assert torch.equal(out, e_rt.attention(qin)), i
+        want = e_rt.attention(qin)
+        if e_rt.tail_len == 0:
+            # The step that completes a page attends it from the codes it just encoded
+            # (float32 products) instead of through the page pass (float16 products).
+            assert (out.float() - want.float()).abs().max().item() <= ATOL, i
+        else:
+            assert torch.equal(out, want), i
     assert g_rt.read_device_error() == 0
     assert g_rt.actual_seq_len == 140 and g_rt.n_pages == 2 and g_rt.tail_len == 12
 

@@ -20,7 +20,7 @@ STATE_WORDS = 6
 
 EXPORTED = (
     "tp_row_bytes", "tp_encode_pages", "tp_append", "tp_decode_attention_workspace_size",
-    "tp_decode_attention", "tp_decode_attention_noalloc", "tp_combine_partials", "tp_fused_scores", "tp_decode_pages",
+    "tp_decode_attention", "tp_decode_step", "tp_decode_attention_noalloc", "tp_combine_partials", "tp_fused_scores", "tp_decode_pages",
     "tp_export_pages", "tp_import_pages", "tp_last_error", "tp_version",
 )
 
@@ -60,6 +60,8 @@ def _declare(lib):
         "tp_decode_attention_workspace_size": (SZ, [I32, I32]),
         "tp_decode_attention": (ctypes.c_int, [ctypes.POINTER(PagePool), ctypes.POINTER(Tail), State, P, P, I32, I32,
                                                F, P, P, P, SZ, P]),
+        "tp_decode_step": (ctypes.c_int, [ctypes.POINTER(PagePool), ctypes.POINTER(Tail), P, P, P, I32, I64, P, I32,
+                                          I32, F, P, P, P, SZ, P]),
         "tp_decode_attention_noalloc": (ctypes.c_int, [ctypes.POINTER(PagePool), ctypes.POINTER(Tail), State, P, P,
                                                        I32, I32, F, P, P, P]),
         "tp_combine_partials": (ctypes.c_int, [P, I32, I32, P, P]),

@@ -286,6 +286,58 @@ class TurboPolarKVCacheRuntime:
             ws.data_ptr(), ws.numel(), _stream(self.device)))
         return out if out is not None else partial_out
 
+    def decode_step(self, k_new: torch.Tensor, v_new: torch.Tensor, q: torch.Tensor, scale: Optional[float] = None,
+                    out: Optional[torch.Tensor] = None, partial_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """``append(k_new, v_new)`` of one token then ``attention(q)``, as one tp_decode_step
+        call (two kernels, no separate append kernel).  Same validation, results and host
+        counters as the two calls; inputs of more than one token take that two-call path."""
+        if k_new.dim() != 4 or k_new.shape[2] != 1 or not self._initialized or k_new.shape != v_new.shape:
+            self.append(k_new, v_new)
+            return self.attention(q, scale=scale, out=out, partial_out=partial_out)
+        self._validate_append_inputs(k_new, v_new)
+        if q.dim() == 4:
+            if q.shape[2] != 1:
+                raise ValueError("decode attention only supports a single query token")
+            q = q.squeeze(2)
+        if q.dim() != 3 or q.shape[0] != self._batch_size or q.shape[-1] != self._head_dim:
+            raise ValueError(f"query shape {tuple(q.shape)} does not match the cache (B={self._batch_size}, D=128)")
+        if q.dtype not in (torch.float16, torch.float32):
+            raise ValueError(f"query dtype must be float16 or float32, got {q.dtype}")
+        if q.device != self.device:
+            raise ValueError("query must be on the cache's device")
+        B, Hq, D = q.shape
+        if Hq % self._num_kv_heads:
+            raise ValueError(f"decode_attention requires GQA ratio to divide evenly, got {Hq} and {self._num_kv_heads}")
+        fills = self.tail_len == PAGE - 1
+        if fills:
+            self._ensure_capacity(self.n_pages + 1)
+        kf = k_new.reshape(self.heads, D)
+        vf = v_new.reshape(self.heads, D)
+        if kf.stride() != vf.stride() or kf.stride(-1) != 1 or kf.stride(0) % 8 or kf.data_ptr() % 16 \
+                or vf.data_ptr() % 16:
+            kf, vf = kf.contiguous(), vf.contiguous()
+        qf = q.reshape(B * Hq, D)
+        if not qf.is_contiguous():
+            qf = qf.contiguous()
+        if out is None and partial_out is None:
+            out = torch.empty((B, Hq, D), dtype=torch.float16, device=self.device)
+        ws = self._workspace_for(B * Hq)
+        scale = float(self.config.attention_scale if scale is None else scale)
+        _lib.check(_lib.lib().tp_decode_step(
+            ctypes.byref(self.pool_struct()), ctypes.byref(self.tail_struct()), self.d_state.data_ptr(),
+            kf.data_ptr(), vf.data_ptr(), _lib.TP_F16 if kf.dtype == torch.float16 else _lib.TP_F32, kf.stride(0),
+            qf.data_ptr(), _lib.TP_F16 if qf.dtype == torch.float16 else _lib.TP_F32, B * Hq, scale,
+            out.data_ptr() if out is not None else None,
+            partial_out.data_ptr() if partial_out is not None else None,
+            ws.data_ptr(), ws.numel(), _stream(self.device)))
+        self.actual_seq_len += 1
+        if fills:
+            self.tail_len = 0
+            self._flushed(1)
+        else:
+            self.tail_len += 1
+        return out if out is not None else partial_out
+
     # ------------------------------------------------------------------ reference views
     def _views(self, n: int):
         """Reference-layout copies of pages [0, n) (``storage.py:89-102, :160-169``)."""

@@ -34,7 +34,7 @@
 #include <cmath>
 #include <mutex>
 
-#include "tp_common.cuh"
+#include "tp_codec.cuh"
 
 namespace tp {
 
@@ -56,15 +56,22 @@ struct AttnParams {
   int page_capacity;
   int l1_bits, deep_bits, l1_pairs, l1_row, deep_row, radii_row, int8_radii;
   int radii_page, l1_page, deep_page;  // bytes per page per head
-  const void* tail_k;
-  const void* tail_v;
+  void* tail_k;
+  void* tail_v;
   int tail_f32;
   tp_state st;
-  const int32_t* d_state;
+  int32_t* d_state;  // written only by the fused step
   const void* q;
   int q_f32;
   int num_q_heads, num_kv_heads, group, nqc, gmax;
   int main_grid;  // CTAs of the page pass
+  // Fused decode step: one new token per KV head (k_new/v_new, tail dtype, heads
+  // new_head_stride elements apart) appended before attention; wpool is the writable pool.
+  int fused;
+  const void* k_new;
+  const void* v_new;
+  int64_t new_head_stride;
+  PoolArgs wpool;
   float scale_log2;
   __half* out;
   float* partial_out;
@@ -527,63 +534,79 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
 }
 
 // Merge the per-CTA partials of one query head -- from the CTAs whose unit ranges cover its
-// (KV head, query chunk) -- and write the output.  One CTA per query head, thread d = channel.
-// Launched as a programmatic dependent of the attention grid: its CTAs become resident while
-// that grid finishes and griddepcontrol.wait releases them once the grid has completed and its
-// memory is visible, so no fence or atomic sits on the path.  Contributor records are staged in
+// (KV head, query chunk) -- with the partial of the tokens after the pages, and write the
+// output.  One CTA per query head; thread d < 128 owns channel d of the merge.  Launched as a
+// programmatic dependent of the page pass: its CTAs become resident while that grid runs (they
+// share the SM with a page-pass CTA) and compute the dense-tail partial then;
+// griddepcontrol.wait releases them once the page pass has completed and its memory is
+// visible, so no fence or atomic sits on the merge path.  Contributor records are staged in
 // shared memory by concurrent 8-byte cp.async copies (one memory round trip per 64 records).
-constexpr int kCombineThreads = kD;
+//
+// Fused decode step (P.fused): the kernel also appends the new token of every KV head, as
+// TurboPolarKVCacheRuntime.append does before attention (turbo_polar_cache.py:106-161).
+// Without a flush, the new token joins the dense-tail partial straight from k_new/v_new and
+// one CTA per KV head stores it in the tail.  When it completes the tail's page, every CTA of
+// that KV head encodes the page in shared memory (bit-exact codec, the same for all of them),
+// one stores it as pool page n_pages, and each computes its query head's partial over the
+// page's decoded keys and values.  The state words advance after the merge, written by the
+// last CTA to have read them (a ticket in d_state[5]), so no CTA of this launch can see the
+// new state.
+constexpr int kCombineThreads = 256;
+constexpr int kCombineWarps = kCombineThreads / 32;
 constexpr int kCombineChunk = 64;
 
 __device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(smem_u32(smem)), "l"(gmem));
 }
 
-// Softmax partial of one query head over the dense tail of its KV head (at most 64 float16 or
-// float32 tokens, the reference's partial block; metal.py:305-321 treats them as plain keys
-// and values).  Warp w owns tokens w, w+4, ..., w+60; lane owns channels 4*lane..4*lane+3.
-// Every load of a warp is issued before any is used (one round trip for K, one for V).
-// Returns (m, l, o[channel tid]) in the base-2 domain; reads only data written before the
-// attention grid started.
 template <typename T>
-__device__ __forceinline__ float4 load4(const void* base, int64_t idx) {
-  if (sizeof(T) == 4) return reinterpret_cast<const float4*>(static_cast<const float*>(base) + idx)[0];
-  const uint2 u = reinterpret_cast<const uint2*>(static_cast<const __half*>(base) + idx)[0];
+__device__ __forceinline__ float4 load4(const T* p) {
+  if (sizeof(T) == 4) return *reinterpret_cast<const float4*>(p);
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
   const float2 a = __half22float2(u32_as_h2(u.x)), b = __half22float2(u32_as_h2(u.y));
   return make_float4(a.x, a.y, b.x, b.y);
 }
 
-template <typename T>
-__device__ void tail_partial(const AttnParams& P, int kvh, int qh, int valid, float* s_sc, float* s_o, float& m_out,
-                             float& l_out, float& o_out) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  constexpr int kWarpsC = kCombineThreads / 32, kPer = kPage / kWarpsC;
-  const int64_t head0 = int64_t(kvh) * kPage * kD;
-  // Query as the kernels read it: float16 (a float32 query is rounded).
+// Query head qh as the kernels read it: float16 (a float32 query is rounded), channels
+// 4*lane .. 4*lane+3.
+__device__ __forceinline__ float4 load_q4(const AttnParams& P, int qh, int lane) {
   const int64_t qi = int64_t(qh) * kD + 4 * lane;
-  float4 q4 = P.q_f32 ? load4<float>(P.q, qi) : load4<__half>(P.q, qi);
-  if (P.q_f32) {
-    q4.x = __half2float(__float2half_rn(q4.x)); q4.y = __half2float(__float2half_rn(q4.y));
-    q4.z = __half2float(__float2half_rn(q4.z)); q4.w = __half2float(__float2half_rn(q4.w));
-  }
-  float4 kv[kPer];
+  if (!P.q_f32) return load4(static_cast<const __half*>(P.q) + qi);
+  float4 q4 = load4(static_cast<const float*>(P.q) + qi);
+  q4.x = __half2float(__float2half_rn(q4.x)); q4.y = __half2float(__float2half_rn(q4.y));
+  q4.z = __half2float(__float2half_rn(q4.z)); q4.w = __half2float(__float2half_rn(q4.w));
+  return q4;
+}
+
+// Softmax partial of one query head over at most 64 tokens whose keys and values `kv(t, lane,
+// k, v)` produces (channels 4*lane .. 4*lane+3 of token t).  Warp w owns tokens w, w+8, ...,
+// w+56; every key of a warp is fetched before any is used.  Returns (m, l, o[channel tid]) in
+// the base-2 domain for tid < 128.  metal.py:305-321 treats these tokens as plain keys and
+// values.
+template <class KV>
+__device__ __forceinline__ void block_partial(const AttnParams& P, int qh, int valid, KV kv, float* s_sc, float* s_o,
+                                              float& m_out, float& l_out, float& o_out) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int kPer = kPage / kCombineWarps;
+  const float4 q4 = load_q4(P, qh, lane);
+  float4 x[kPer];  // keys, then values
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
-    const int t = warp + kWarpsC * j;
-    kv[j] = t < valid ? load4<T>(P.tail_k, head0 + int64_t(t) * kD + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const int t = warp + kCombineWarps * j;
+    x[j] = t < valid ? kv(t, lane, true) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
-    float dot = q4.x * kv[j].x + q4.y * kv[j].y + q4.z * kv[j].z + q4.w * kv[j].w;
+    float dot = q4.x * x[j].x + q4.y * x[j].y + q4.z * x[j].z + q4.w * x[j].w;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    const int t = warp + kWarpsC * j;
+    const int t = warp + kCombineWarps * j;
     if (lane == 0 && t < valid) s_sc[t] = dot * P.scale_log2;
   }
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
-    const int t = warp + kWarpsC * j;
-    kv[j] = t < valid ? load4<T>(P.tail_v, head0 + int64_t(t) * kD + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const int t = warp + kCombineWarps * j;
+    x[j] = t < valid ? kv(t, lane, false) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   __syncthreads();
   float m = -INFINITY;
@@ -592,61 +615,233 @@ __device__ void tail_partial(const AttnParams& P, int kvh, int qh, int valid, fl
   float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
-    const int t = warp + kWarpsC * j;
+    const int t = warp + kCombineWarps * j;
     if (t < valid) {
       const float p = exp2_approx(s_sc[t] - m);
       l += p;
-      o4.x = fmaf(p, kv[j].x, o4.x); o4.y = fmaf(p, kv[j].y, o4.y);
-      o4.z = fmaf(p, kv[j].z, o4.z); o4.w = fmaf(p, kv[j].w, o4.w);
+      o4.x = fmaf(p, x[j].x, o4.x); o4.y = fmaf(p, x[j].y, o4.y);
+      o4.z = fmaf(p, x[j].z, o4.z); o4.w = fmaf(p, x[j].w, o4.w);
     }
   }
   reinterpret_cast<float4*>(s_o + warp * kD)[lane] = o4;
   if (lane == 0) s_sc[kPage + warp] = l;
   __syncthreads();
-  float o = 0.f;
-  l = 0.f;
+  if (tid < kD) {
+    float o = 0.f;
+    l = 0.f;
 #pragma unroll
-  for (int w = 0; w < kWarpsC; ++w) {
-    o += s_o[w * kD + tid];
-    l += s_sc[kPage + w];
+    for (int w = 0; w < kCombineWarps; ++w) {
+      o += s_o[w * kD + tid];
+      l += s_sc[kPage + w];
+    }
+    m_out = m;
+    l_out = l;
+    o_out = o;
   }
-  m_out = m;
-  l_out = l;
-  o_out = o;
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kCombineThreads) split_combine_kernel(const __grid_constant__ AttnParams P) {
-  __shared__ __align__(16) float recs[kCombineChunk][TP_PARTIAL_FLOATS];
+// One page of one KV head held in shared memory in the pool layout (the fused step's flush).
+struct SmemPage {
+  uint8_t codes[kPage * kPairs];     // encode scratch: one code per pair
+  float red[8];                      // encode scratch: block reduction
+  __align__(16) uint8_t radii[kPage * kPairs * 2];
+  __align__(16) uint8_t angles[kPage * kPairs];  // level-1 rows, then deep rows
+  __align__(16) uint8_t v_codes[kVCodesPage];
+  __align__(16) __half v_scales[kPage * 4];
+  __half radii_scale;
+};
+
+union CombineSmem {
+  float recs[kCombineChunk][TP_PARTIAL_FLOATS];
+  SmemPage page;
+};
+
+// Key and value channels 4*lane .. 4*lane+3 of token t of the shared-memory page, decoded as
+// rfsn_v11/quant/polar/decoder.py:36-67 and v_quant/encoder.py:32-38 do (cos and sin of the
+// code angle from the float16 table the page pass uses).
+__device__ __forceinline__ float4 page_token(const AttnParams& P, const SmemPage& pg, int t, int lane, bool key) {
+  if (!key) {
+    float vx[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int d = 4 * lane + e;
+      const int8_t code = int8_t(pg.v_codes[vcode_offset(t, d)] ^ 0x80u);
+      vx[e] = __half2float(__float2half_rn(float(code) * __half2float(pg.v_scales[vscale_index(t, d >> 5)])));
+    }
+    return make_float4(vx[0], vx[1], vx[2], vx[3]);
+  }
+  float kx[4];
+  const uint32_t* lut = P.lut;
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int j = 2 * lane + e;
+    uint32_t code, cs;
+    if (j < P.l1_pairs) {
+      const uint8_t* row = pg.angles + t * P.l1_row;
+      code = P.l1_bits == 8 ? row[j] : (row[j >> 1] >> (4 * (j & 1))) & 15u;
+      cs = lut[code];
+    } else {
+      const uint8_t* row = pg.angles + kPage * P.l1_row + t * P.deep_row;
+      const int rel = j - P.l1_pairs;
+      if (P.deep_bits == 8) code = row[rel];
+      else if (P.deep_bits == 4) code = (row[rel >> 1] >> (4 * (rel & 1))) & 15u;
+      else code = (row[rel >> 2] >> (2 * (rel & 3))) & 3u;
+      cs = lut[kLutEntries + code];
+    }
+    float r;
+    if (P.int8_radii) {
+      r = expf(float(reinterpret_cast<const int8_t*>(pg.radii)[t * kPairs + j]) * __half2float(pg.radii_scale));
+    } else {
+      r = __half2float(*reinterpret_cast<const __half*>(pg.radii + radii_f16_offset(t, j)));
+    }
+    const float2 c2 = __half22float2(u32_as_h2(cs));
+    kx[2 * e] = __half2float(__float2half_rn(r * c2.x));
+    kx[2 * e + 1] = __half2float(__float2half_rn(r * c2.y));
+  }
+  return make_float4(kx[0], kx[1], kx[2], kx[3]);
+}
+
+// Copy the encoded shared-memory page to pool page `page` of KV head kvh.
+__device__ __forceinline__ void store_page(const AttnParams& P, const SmemPage& pg, int kvh, int page) {
+  const PagePtrs dst = P.wpool.page(kvh, page);
+  const int rb = kPage * P.radii_row, lb = kPage * P.l1_row, db = kPage * P.deep_row;
+  for (int i = threadIdx.x; i < rb / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(dst.radii)[i] = reinterpret_cast<const uint4*>(pg.radii)[i];
+  for (int i = threadIdx.x; i < lb; i += blockDim.x) dst.l1[i] = pg.angles[i];
+  for (int i = threadIdx.x; i < db; i += blockDim.x) dst.deep[i] = pg.angles[lb + i];
+  for (int i = threadIdx.x; i < int(kVCodesPage / 16); i += blockDim.x)
+    reinterpret_cast<uint4*>(dst.v_codes)[i] = reinterpret_cast<const uint4*>(pg.v_codes)[i];
+  for (int i = threadIdx.x; i < int(kVScalesPage / 16); i += blockDim.x)
+    reinterpret_cast<uint4*>(dst.v_scales)[i] = reinterpret_cast<const uint4*>(pg.v_scales)[i];
+  if (threadIdx.x == 0 && P.int8_radii) *dst.radii_scale = pg.radii_scale;
+}
+
+template <typename T>
+__device__ __forceinline__ void dense_tail_partial(const AttnParams& P, int kvh, int qh, int valid, int new_at,
+                                                   float* s_sc, float* s_o, float& M, float& L, float& O) {
+  const T* tk = static_cast<const T*>(P.tail_k) + int64_t(kvh) * kPage * kD;
+  const T* tv = static_cast<const T*>(P.tail_v) + int64_t(kvh) * kPage * kD;
+  const T* nk = static_cast<const T*>(P.k_new) + int64_t(kvh) * P.new_head_stride;
+  const T* nv = static_cast<const T*>(P.v_new) + int64_t(kvh) * P.new_head_stride;
+  block_partial(P, qh, valid, [&](int t, int lane, bool key) {
+    const bool nw = t == new_at;
+    return key ? load4((nw ? nk : tk + t * kD) + 4 * lane) : load4((nw ? nv : tv + t * kD) + 4 * lane);
+  }, s_sc, s_o, M, L, O);
+}
+
+// Kept out of line: the page encode needs more registers than the merge path may use.
+template <typename T>
+__device__ __noinline__ float3 flush_partial(const AttnParams& P, CombineSmem& sm, int kvh, int qh, int page,
+                                              bool store, int valid, float* s_sc, float* s_o) {
+  SmemPage& pg = sm.page;
+  PagePtrs dst;
+  dst.radii = pg.radii;
+  dst.radii_scale = &pg.radii_scale;
+  dst.l1 = pg.angles;
+  dst.deep = pg.angles + kPage * P.l1_row;
+  dst.v_codes = reinterpret_cast<int8_t*>(pg.v_codes);
+  dst.v_scales = pg.v_scales;
+  const T* tk = static_cast<const T*>(P.tail_k) + int64_t(kvh) * kPage * kD;
+  const T* tv = static_cast<const T*>(P.tail_v) + int64_t(kvh) * kPage * kD;
+  encode_page<T>(tk, tv, kD, dst, P.wpool, pg.codes, pg.red, pg.v_codes, pg.v_scales,
+                 static_cast<const T*>(P.k_new) + int64_t(kvh) * P.new_head_stride,
+                 static_cast<const T*>(P.v_new) + int64_t(kvh) * P.new_head_stride);
+  __syncthreads();
+  if (store) store_page(P, pg, kvh, page);
+  float M = -INFINITY, L = 0.f, O = 0.f;
+  block_partial(P, qh, valid, [&](int t, int lane, bool key) { return page_token(P, pg, t, lane, key); }, s_sc, s_o,
+                M, L, O);
+  return make_float3(M, L, O);
+}
+
+// Fused step: advance the state words once every CTA has read them (ticket) and the page pass
+// has completed (griddepcontrol.wait), then reset the ticket.
+__device__ __forceinline__ void advance_state(const AttnParams& P, const tp_state& st, int n_pages, int tail_len,
+                                              bool appended, bool flush) {
+  if (appended) {
+    P.d_state[0] = n_pages + (flush ? 1 : 0);
+    P.d_state[1] = flush ? 0 : tail_len + 1;
+    P.d_state[2] = st.seq_len + 1;
+  }
+  P.d_state[5] = 0;
+}
+
+// At most 64 registers a thread, so a split-combine CTA fits beside a page-pass CTA (177).
+__global__ void __launch_bounds__(kCombineThreads, 4) split_combine_kernel(const __grid_constant__ AttnParams P) {
+  __shared__ __align__(16) CombineSmem sm;
   __shared__ int soff[kMaxContrib];
-  __shared__ __align__(16) float s_o[(kCombineThreads / 32) * kD];
-  __shared__ float s_sc[kPage + kCombineThreads / 32];
+  __shared__ __align__(16) float s_o[kCombineWarps * kD];
+  __shared__ float s_sc[kPage + kCombineWarps];
+  __shared__ int s_last;
   const int tid = threadIdx.x;
   const int vh = blockIdx.x / P.gmax, h = blockIdx.x % P.gmax;
   const int kvh = vh / P.nqc, chunk = vh % P.nqc;
   const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
-  if (h >= gc) {
-    asm volatile("griddepcontrol.wait;\n" ::: "memory");
-    return;
+
+  // One thread reads the state words; with the fused step it then takes a ticket, and the
+  // CTA holding the last ticket advances the words after the merge.
+  __shared__ tp_state s_st;
+  if (tid == 0) {
+    tp_state st = P.st;
+    if (P.d_state) {
+      st.n_pages = P.d_state[0];
+      st.tail_len = P.d_state[1];
+      st.seq_len = P.d_state[2];
+      st.first_page = P.d_state[3];
+    }
+    s_st = st;
+    s_last = 0;
+    if (P.fused) {
+      __threadfence();  // the reads above happen before the ticket
+      s_last = atomicAdd(&P.d_state[5], 1) == int(gridDim.x) - 1;
+    }
   }
-  const int qh = kvh * P.group + chunk * kMaxHeads + h;
-  // The dense tail first, overlapped with the attention grid (its inputs predate that grid).
-  tp_state st = P.st;
-  if (P.d_state) {
-    st.n_pages = P.d_state[0];
-    st.tail_len = P.d_state[1];
-    st.seq_len = P.d_state[2];
-    st.first_page = P.d_state[3];
-  }
+  __syncthreads();
+  const tp_state st = s_st;
   const int n_pages = min(max(st.n_pages, 0), P.page_capacity);
   const int tail_len = min(max(st.tail_len, 0), kPage);
   const int64_t tpos0 = (int64_t(st.first_page) + n_pages) * kPage;
-  const int valid = int(clamp64(int64_t(st.seq_len) - tpos0, 0, tail_len));
-  float M = -INFINITY, L = 0.f, O = 0.f;
-  if (valid > 0) {
-    if (P.tail_f32) tail_partial<float>(P, kvh, qh, valid, s_sc, s_o, M, L, O);
-    else tail_partial<__half>(P, kvh, qh, valid, s_sc, s_o, M, L, O);
+  // Fused step: the new token goes to tail index tail_len; it completes a page when that is 63.
+  const bool flush = P.fused && tail_len == kPage - 1;
+  const bool appended = P.fused && tail_len < kPage && !(flush && n_pages >= P.page_capacity);
+  if (h >= gc) {
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    if (s_last && tid == 0) advance_state(P, st, n_pages, tail_len, appended, flush);
+    return;
   }
+  const int qh = kvh * P.group + chunk * kMaxHeads + h;
+  const bool designated = chunk == 0 && h == 0;
+  float M = -INFINITY, L = 0.f, O = 0.f;
+  if (appended && flush) {
+    const int valid = int(clamp64(int64_t(st.seq_len) + 1 - tpos0, 0, kPage));
+    const float3 r = P.tail_f32 ? flush_partial<float>(P, sm, kvh, qh, n_pages, designated, valid, s_sc, s_o)
+                                : flush_partial<__half>(P, sm, kvh, qh, n_pages, designated, valid, s_sc, s_o);
+    M = r.x;
+    L = r.y;
+    O = r.z;
+  } else {
+    const int len = tail_len + (appended ? 1 : 0);
+    const int valid = int(clamp64(int64_t(st.seq_len) + (appended ? 1 : 0) - tpos0, 0, len));
+    const int new_at = appended ? tail_len : -1;
+    if (valid > 0) {
+      if (P.tail_f32) dense_tail_partial<float>(P, kvh, qh, valid, new_at, s_sc, s_o, M, L, O);
+      else dense_tail_partial<__half>(P, kvh, qh, valid, new_at, s_sc, s_o, M, L, O);
+    }
+    if (appended && designated) {
+      const int esz = P.tail_f32 ? 4 : 2;
+      const uint8_t* nk = static_cast<const uint8_t*>(P.k_new) + int64_t(kvh) * P.new_head_stride * esz;
+      const uint8_t* nv = static_cast<const uint8_t*>(P.v_new) + int64_t(kvh) * P.new_head_stride * esz;
+      uint8_t* tk = static_cast<uint8_t*>(P.tail_k) + (int64_t(kvh) * kPage + tail_len) * kD * esz;
+      uint8_t* tv = static_cast<uint8_t*>(P.tail_v) + (int64_t(kvh) * kPage + tail_len) * kD * esz;
+      for (int i = tid; i < kD * esz / 4; i += kCombineThreads) {
+        reinterpret_cast<uint32_t*>(tk)[i] = reinterpret_cast<const uint32_t*>(nk)[i];
+        reinterpret_cast<uint32_t*>(tv)[i] = reinterpret_cast<const uint32_t*>(nv)[i];
+      }
+    }
+  }
+  // Token dropped: 1 = tail state out of range, 2 = page pool full.
+  if (P.fused && !appended && tid == 0 && designated) P.d_state[4] = tail_len >= kPage ? 1 : 2;
 
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
   // The page pass's partition, recomputed from the same state it read.
@@ -666,30 +861,33 @@ __global__ void __launch_bounds__(kCombineThreads) split_combine_kernel(const __
       const int cn = min(kCombineChunk, n - c0);
       for (int i = tid; i < cn * (TP_PARTIAL_FLOATS / 2); i += kCombineThreads) {
         const int ci = i / (TP_PARTIAL_FLOATS / 2), e = 2 * (i - ci * (TP_PARTIAL_FLOATS / 2));
-        cp_async8(&recs[ci][e], P.ws_partials + soff[c0 + ci] + e);
+        cp_async8(&sm.recs[ci][e], P.ws_partials + soff[c0 + ci] + e);
       }
       cp_async_commit();
       cp_async_wait<0>();
       __syncthreads();
-      float Mc = M;
-      for (int ci = 0; ci < cn; ++ci) Mc = fmaxf(Mc, recs[ci][0]);
-      if (Mc != -INFINITY) {
-        const float a = (M == -INFINITY) ? 0.f : exp2_approx(M - Mc);
-        L *= a;
-        O *= a;
+      if (tid < kD) {
+        float Mc = M;
+        for (int ci = 0; ci < cn; ++ci) Mc = fmaxf(Mc, sm.recs[ci][0]);
+        if (Mc != -INFINITY) {
+          const float a = (M == -INFINITY) ? 0.f : exp2_approx(M - Mc);
+          L *= a;
+          O *= a;
 #pragma unroll 4
-        for (int ci = 0; ci < cn; ++ci) {
-          const float m = recs[ci][0];
-          const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - Mc);
-          L = fmaf(recs[ci][1], w, L);
-          O = fmaf(recs[ci][2 + tid], w, O);
+          for (int ci = 0; ci < cn; ++ci) {
+            const float m = sm.recs[ci][0];
+            const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - Mc);
+            L = fmaf(sm.recs[ci][1], w, L);
+            O = fmaf(sm.recs[ci][2 + tid], w, O);
+          }
+          M = Mc;
         }
-        M = Mc;
       }
       __syncthreads();
     }
   }
-  write_result(P, qh, tid, M, L, O);
+  if (tid < kD) write_result(P, qh, tid, M, L, O);
+  if (s_last && tid == 0) advance_state(P, st, n_pages, tail_len, appended, flush);
 }
 
 // ----------------------------------------------------------------------------- cross-shard combine
@@ -758,9 +956,17 @@ size_t tp_decode_attention_workspace_size(int32_t num_kv_heads, int32_t num_q_he
   return (bytes + 255) & ~size_t(255);
 }
 
-int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state state, const int32_t* d_state,
-                        const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
-                        float* partial_out, void* workspace, size_t workspace_bytes, void* stream) {
+// The new token of a fused decode step.
+struct StepArgs {
+  const void* k_new;
+  const void* v_new;
+  int64_t head_stride;
+};
+
+static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state state, int32_t* d_state,
+                         const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
+                         float* partial_out, void* workspace, size_t workspace_bytes, void* stream,
+                         const StepArgs* step) {
   Layout L;
   int st = validate_pool(pool, &L);
   if (st != TP_OK) return st;
@@ -824,6 +1030,11 @@ int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state 
   P.main_grid = grid;
   if (grid > kMaxContrib) return fail(TP_ERR_UNSUPPORTED, "tp_decode_attention: too many KV heads for one launch");
   P.ws_error = static_cast<int*>(workspace);  // word 0: error
+  P.fused = step != nullptr;
+  P.k_new = step ? step->k_new : nullptr;
+  P.v_new = step ? step->v_new : nullptr;
+  P.new_head_stride = step ? step->head_stride : 0;
+  P.wpool = pool_args(*pool, L);
   P.ws_partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
   // Half-page stage: radii | v codes | level-1 codes | 64-byte bank shift | deep codes | v scales.
   auto up = [](int x, int a) { return (x + a - 1) / a * a; };
@@ -879,6 +1090,33 @@ int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state 
   const cudaError_t e = cudaLaunchKernelEx(&cfg, split_combine_kernel, P);
   if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_decode_attention (combine): ") + cudaGetErrorString(e));
   return TP_OK;
+}
+
+int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state state, const int32_t* d_state,
+                        const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
+                        float* partial_out, void* workspace, size_t workspace_bytes, void* stream) {
+  // Without a step the kernels only read the state words.
+  return run_attention(pool, tail, state, const_cast<int32_t*>(d_state), q, q_dtype, num_q_heads, scale, out,
+                       partial_out, workspace, workspace_bytes, stream, nullptr);
+}
+
+int tp_decode_step(const tp_page_pool* pool, const tp_tail* tail, int32_t* d_state, const void* k_new,
+                   const void* v_new, int32_t kv_dtype, int64_t head_stride, const void* q, int32_t q_dtype,
+                   int32_t num_q_heads, float scale, void* out, float* partial_out, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  if (!d_state) return fail(TP_ERR_INVALID, "tp_decode_step: the state words are required");
+  if (!pool || !tail) return fail(TP_ERR_INVALID, "tp_decode_step: NULL pool or tail");
+  if (!k_new || !v_new) return fail(TP_ERR_INVALID, "tp_decode_step: NULL new token");
+  if (kv_dtype != tail->dtype) return fail(TP_ERR_INVALID, "tp_decode_step: new token dtype must match the tail");
+  if (kv_dtype != TP_F16 && kv_dtype != TP_F32) return fail(TP_ERR_INVALID, "only float16 and float32 inputs are supported");
+  const int64_t esz = kv_dtype == TP_F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(k_new) & 15) || (reinterpret_cast<uintptr_t>(v_new) & 15) ||
+      head_stride < kD || (head_stride * esz) % 16)
+    return fail(TP_ERR_INVALID, "tp_decode_step: new token rows must be 16-byte aligned, heads >= 128 elements apart");
+  StepArgs a{k_new, v_new, head_stride};
+  tp_state none = {0, 0, 0, 0};
+  return run_attention(pool, tail, none, d_state, q, q_dtype, num_q_heads, scale, out, partial_out, workspace,
+                       workspace_bytes, stream, &a);
 }
 
 // ----------------------------------------------------------------------------- no-allocation variant

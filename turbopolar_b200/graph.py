@@ -1,8 +1,8 @@
 """CUDA-graph capture of decode steps.
 
-A decode step of one cache layer is ``append(1 token) + attention(q)``.  Both kernels read
-the cache counters from the runtime's device state words and the append kernel advances them,
-so one captured graph replays correctly at every sequence position.  The host mirror of the
+A decode step of one cache layer is ``append(1 token) + attention(q)``, one tp_decode_step
+call: its kernels read the cache counters from the runtime's device state words and advance
+them, so one captured graph replays correctly at every sequence position.  The host mirror of the
 counters is advanced on each replay with the same deterministic rule the append kernel uses.
 
 Requirements: the runtime was created with ``max_seq_len`` (the pool never grows while a
@@ -39,6 +39,25 @@ def launch_attention(rt: TurboPolarKVCacheRuntime, q: torch.Tensor, out: Optiona
     _lib.check(_lib.lib().tp_decode_attention(
         ctypes.byref(rt.pool_struct()), ctypes.byref(rt.tail_struct()), rt.state(), rt.d_state.data_ptr(),
         q.data_ptr(), _lib.TP_F16 if q.dtype == torch.float16 else _lib.TP_F32, B * Hq, float(scale),
+        out.data_ptr() if out is not None else None, partial_out.data_ptr() if partial_out is not None else None,
+        ws.data_ptr(), ws.numel(), torch.cuda.current_stream(q.device).cuda_stream))
+
+
+def launch_decode_step(rt: TurboPolarKVCacheRuntime, k: torch.Tensor, v: torch.Tensor, q: torch.Tensor,
+                       out: Optional[torch.Tensor], scale: float, partial_out: Optional[torch.Tensor] = None) -> None:
+    """Enqueue tp_decode_step (append one token ``(B, H_kv, 1, 128)``, then attend) on the
+    device counters."""
+    B, H, T, D = k.shape
+    kf = k.reshape(B * H, D)
+    vf = v.reshape(B * H, D)
+    if kf.stride() != vf.stride() or kf.stride(-1) != 1:
+        raise ValueError("new K and V rows must share one layout with contiguous channels")
+    Bq, Hq = q.shape[0], q.shape[-2]
+    ws = rt._workspace_for(Bq * Hq)
+    _lib.check(_lib.lib().tp_decode_step(
+        ctypes.byref(rt.pool_struct()), ctypes.byref(rt.tail_struct()), rt.d_state.data_ptr(), kf.data_ptr(),
+        vf.data_ptr(), _lib.TP_F16 if k.dtype == torch.float16 else _lib.TP_F32, kf.stride(0), q.data_ptr(),
+        _lib.TP_F16 if q.dtype == torch.float16 else _lib.TP_F32, Bq * Hq, float(scale),
         out.data_ptr() if out is not None else None, partial_out.data_ptr() if partial_out is not None else None,
         ws.data_ptr(), ws.numel(), torch.cuda.current_stream(q.device).cuda_stream))
 
@@ -86,8 +105,7 @@ class DecodeStep:
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             for (r, k, v, q, o), s in zip(layers, self.scales):
-                launch_append(r, k, v)
-                launch_attention(r, q, o, s)
+                launch_decode_step(r, k, v, q, o, s)
             if extra is not None:
                 extra()
 

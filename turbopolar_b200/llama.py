@@ -100,13 +100,11 @@ class TurboPolarFastCache(CacheLayerMixin):
             k_new = k_new.to(torch.float16)
         if v_new.dtype != torch.float16:
             v_new = v_new.to(torch.float16)
-        self.runtime.append(k_new, v_new)
-        if self.runtime.actual_seq_len == 0:
-            raise RuntimeError("TurboPolar cache returned no blocks after append")
         q_squeezed = q.squeeze(2)
         if q_squeezed.dtype not in (torch.float16, torch.float32):
             q_squeezed = q_squeezed.to(torch.float16)
-        return self.runtime.attention(q_squeezed, scale=scale)
+        # Append and attention in one tp_decode_step call.
+        return self.runtime.decode_step(k_new, v_new, q_squeezed, scale=scale)
 
     def size(self) -> int:
         return self.offset

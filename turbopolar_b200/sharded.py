@@ -52,9 +52,9 @@ def sharded_attention(rt: TurboPolarKVCacheRuntime, q: torch.Tensor, group=None)
 
 
 class ShardedDecodeStep:
-    """One captured decode step over all layers: (last rank) append, local attention partial,
-    NCCL all-gather, combine.  The graph must be released (``release()``) before the process
-    group is destroyed."""
+    """One captured decode step over all layers: local attention partial (the last rank appends
+    the new token in the same call, tp_decode_step), NCCL all-gather, combine.  The graph must
+    be released (``release()``) before the process group is destroyed."""
 
     def __init__(self, layers: List[TurboPolarKVCacheRuntime], k_in, v_in, q_in, out, rank: int, world: int,
                  group=None):
@@ -74,8 +74,10 @@ class ShardedDecodeStep:
         with torch.cuda.graph(self.graph):
             for i, rt in enumerate(layers):
                 if self.last:
-                    graph.launch_append(rt, k_in[i], v_in[i])
-                graph.launch_attention(rt, q_in[i], None, rt.config.attention_scale, partial_out=self.partials[i])
+                    graph.launch_decode_step(rt, k_in[i], v_in[i], q_in[i], None, rt.config.attention_scale,
+                                             partial_out=self.partials[i])
+                else:
+                    graph.launch_attention(rt, q_in[i], None, rt.config.attention_scale, partial_out=self.partials[i])
                 dist.all_gather_into_tensor(self.gathered[i], self.partials[i], group=group)
                 combine(self.gathered[i], out[i])
         torch.cuda.synchronize()
