@@ -385,6 +385,49 @@ __device__ __forceinline__ void write_result(const AttnParams& P, int qh, int d,
 }
 
 // ----------------------------------------------------------------------------- kernel
+__device__ __forceinline__ tp_state read_state(const AttnParams& P) {
+  tp_state st = P.st;
+  if (P.d_state) {
+    st.n_pages = P.d_state[0];
+    st.tail_len = P.d_state[1];
+    st.seq_len = P.d_state[2];
+    st.first_page = P.d_state[3];
+  }
+  return st;
+}
+
+// This CTA's share of the page pass: units (half pages, head-major) [u0, u1), at most two
+// heads ("segments"), and warp `warp`'s contiguous slice of each segment.
+struct Part {
+  int n_pages;
+  bool active;
+  int vh_first, nseg, wa0, wn0, wa1, wn1, total;
+};
+
+__device__ __forceinline__ Part make_part(const AttnParams& P, const tp_state& st, int c, int warp) {
+  Part pt = {};
+  pt.n_pages = min(max(st.n_pages, 0), P.page_capacity);
+  const int uph = 2 * pt.n_pages;
+  const int U = P.num_kv_heads * P.nqc * uph;
+  const int C = U < int(gridDim.x) ? U : int(gridDim.x);
+  pt.active = U > 0 && c < C;
+  if (!pt.active) return pt;
+  const int u0 = part_begin(c, C, U), u1 = part_begin(c + 1, C, U);
+  pt.vh_first = u0 / uph;
+  pt.nseg = (u1 - 1) / uph - pt.vh_first + 1;
+  const int hb0 = pt.vh_first * uph;
+  const int a0 = u0 - hb0, n0 = min(u1, hb0 + uph) - u0;
+  pt.wa0 = a0 + (warp * n0) / kWarps;
+  pt.wn0 = a0 + ((warp + 1) * n0) / kWarps - pt.wa0;
+  if (pt.nseg > 1) {
+    const int n1 = u1 - (hb0 + uph);
+    pt.wa1 = (warp * n1) / kWarps;
+    pt.wn1 = ((warp + 1) * n1) / kWarps - pt.wa1;
+  }
+  pt.total = pt.wn0 + pt.wn1;
+  return pt;
+}
+
 template <bool kFast>
 __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __grid_constant__ AttnParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -394,44 +437,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   const int gmax = P.gmax;
   const int rec_stride = gmax * TP_PARTIAL_FLOATS;
 
-  tp_state st = P.st;
-  if (P.d_state) {
-    st.n_pages = P.d_state[0];
-    st.tail_len = P.d_state[1];
-    st.seq_len = P.d_state[2];
-    st.first_page = P.d_state[3];
-  }
-  const int n_pages = min(max(st.n_pages, 0), P.page_capacity);
-  const int tail_len = min(max(st.tail_len, 0), kPage);
-  const int uph = 2 * n_pages;  // the dense tail is handled by split_combine_kernel
-  const int VH = P.num_kv_heads * P.nqc;
-  const int U = VH * uph;
-  const int C = U < int(gridDim.x) ? U : int(gridDim.x);
-  // Let the split-combine grid become resident now; it waits for this grid to complete.
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-  if (U == 0) return;
-  const int c = blockIdx.x;
-  if (c >= C) return;
-  const int u0 = part_begin(c, C, U), u1 = part_begin(c + 1, C, U);
-
-  // Segments of this CTA (at most two heads) and this warp's slice of each.
-  const int vh_first = u0 / uph, vh_last = (u1 - 1) / uph;
-  const int nseg = vh_last - vh_first + 1;
-  int wa0 = 0, wn0 = 0, wa1 = 0, wn1 = 0;
+  // Before the previous kernel in the stream has completed (this grid is its programmatic
+  // dependent): only the code tables and the stage barriers, which depend on nothing it writes.
   {
-    const int hb0 = vh_first * uph;
-    const int a0 = u0 - hb0, n0 = min(u1, hb0 + uph) - u0;
-    wa0 = a0 + (warp * n0) / kWarps;
-    wn0 = a0 + ((warp + 1) * n0) / kWarps - wa0;
-    if (nseg > 1) {
-      const int n1 = u1 - (hb0 + uph);
-      wa1 = (warp * n1) / kWarps;
-      wn1 = ((warp + 1) * n1) / kWarps - wa1;
+    const int n1 = 1 << P.l1_bits, n2 = 1 << P.deep_bits;
+    for (int i = tid; i < n1 + n2; i += kThreads) {
+      const int j = i < n1 ? i : kLutEntries + (i - n1);
+      lut[j] = P.lut[j];
     }
   }
-  const int total = wn0 + wn1;
-  uint8_t* stages = smem + P.smem_stage_off + warp * 2 * P.stage_bytes;
-
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.smem_bar_off) + warp * 2;
   if (lane == 0) {
     mbar_init(&bars[0], 1);
@@ -440,28 +454,68 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   }
   __syncwarp();
   const uint64_t pol = l2_evict_first_policy();
-  // Lane 0 fills stage i&1 for this warp's unit i (a page half) by bulk copy.
+  uint8_t* stages = smem + P.smem_stage_off + warp * 2 * P.stage_bytes;
+  const int c = blockIdx.x;
+
+  // The first two units of every warp go in flight before the wait, on the partition of the
+  // page count read now.  Every page below the newest one was written by a launch that had
+  // completed before the previous kernel in the stream started, so copies of those are valid
+  // whatever that kernel does; the newest page may be the one it is writing (an append that
+  // completed a page), so a warp whose first units touch it waits.  If the previous kernel
+  // changed the page count (it appended to this same cache), the copies are drained and the
+  // units reissued on the new partition.
+  Part pt = make_part(P, read_state(P), c, warp);
+  int seq0 = 0;      // stage-barrier sequence number of this warp's unit 0
+  int issued = 0;    // units of this warp in flight
   auto issue = [&](int i) {
-    if (lane == 0 && i < total) {
-      const bool s1 = i >= wn0;
-      const int j = s1 ? wa1 + (i - wn0) : wa0 + i;
-      issue_half(stages + (i & 1) * P.stage_bytes, &bars[i & 1], P, (vh_first + (s1 ? 1 : 0)) / P.nqc, j >> 1, j & 1,
-                 pol);
+    if (lane == 0 && i < pt.total) {
+      const bool s1 = i >= pt.wn0;
+      const int j = s1 ? pt.wa1 + (i - pt.wn0) : pt.wa0 + i;
+      const int q = seq0 + i;
+      issue_half(stages + (q & 1) * P.stage_bytes, &bars[q & 1], P, (pt.vh_first + (s1 ? 1 : 0)) / P.nqc, j >> 1,
+                 j & 1, pol);
     }
   };
-
-  // The first two units of every warp are in flight before anything else runs.
-  issue(0);
-  issue(1);
+  auto unit_page = [&](int i) {
+    const bool s1 = i >= pt.wn0;
+    return (s1 ? pt.wa1 + (i - pt.wn0) : pt.wa0 + i) >> 1;
+  };
   {
-    const int n1 = 1 << P.l1_bits, n2 = 1 << P.deep_bits;
-    for (int i = tid; i < n1 + n2; i += kThreads) {
-      const int j = i < n1 ? i : kLutEntries + (i - n1);
-      lut[j] = P.lut[j];
+    const int early = min(2, pt.total);
+    bool safe = true;
+    for (int i = 0; i < early; ++i) safe = safe && unit_page(i) < pt.n_pages - 1;
+    if (safe) {
+      issue(0);
+      issue(1);
+      issued = early;
     }
   }
-  __syncthreads();
+
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  // Let the split-combine grid become resident now; it waits for this grid to complete.
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+
+  const tp_state st = read_state(P);
   bool timed_out = false;
+  if (min(max(st.n_pages, 0), P.page_capacity) != pt.n_pages) {
+    for (int k = 0; k < issued; ++k)
+      if (!stage_wait(&bars[k], 0)) timed_out = true;
+    __syncwarp();
+    seq0 = issued;
+    issued = 0;
+    pt = make_part(P, st, c, warp);
+  }
+  if (issued == 0) {
+    issue(0);
+    issue(1);
+  }
+  if (!pt.active) {
+    if (timed_out && lane == 0) atomicExch(P.ws_error, 1);
+    return;
+  }
+  const int vh_first = pt.vh_first, nseg = pt.nseg;
+  const int wa0 = pt.wa0, wn0 = pt.wn0, wa1 = pt.wa1, wn1 = pt.wn1;
+  __syncthreads();  // code tables
   WarpAcc A;
   uint32_t qf[16];
   for (int s = 0; s < nseg; ++s) {
@@ -475,7 +529,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
       acc_reset(A);
     }
     for (int i = i0; i < i0 + wn; ++i) {
-      const bool ready = stage_wait(&bars[i & 1], (i >> 1) & 1);
+      const int q = seq0 + i;
+      const bool ready = stage_wait(&bars[q & 1], (q >> 1) & 1);
       if (!ready) timed_out = true;
       const int j = wa + (i - i0);
       if (!ready) {
@@ -486,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
         const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, kHalf));
         float rs = 0.f;
         if (P.int8_radii) rs = __half2float(P.radii_scales[int64_t(kvh) * P.page_capacity + page]);
-        process_half<kFast>(A, stages + (i & 1) * P.stage_bytes, P, lut, qf, rs, vt, lane);
+        process_half<kFast>(A, stages + (q & 1) * P.stage_bytes, P, lut, qf, rs, vt, lane);
       }
       __syncwarp();
       issue(i + 2);
@@ -778,6 +833,9 @@ __global__ void __launch_bounds__(kCombineThreads, 4) split_combine_kernel(const
   const int vh = blockIdx.x / P.gmax, h = blockIdx.x % P.gmax;
   const int kvh = vh / P.nqc, chunk = vh % P.nqc;
   const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
+  // The next page pass in the stream may start its prologue now; it waits for this grid to
+  // complete before it reads anything.
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
   // One thread reads the state words; with the fused step it then takes a ticket, and the
   // CTA holding the last ticket advances the words after the merge.
@@ -1070,12 +1128,24 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
                                    " bytes of shared memory: " + cudaGetErrorString(e));
     have = smem;
   }
-  if (fast)
-    decode_attention_kernel<true><<<grid, kThreads, smem, s>>>(P);
-  else
-    decode_attention_kernel<false><<<grid, kThreads, smem, s>>>(P);
-  st = check_launch("tp_decode_attention");
-  if (st != TP_OK) return st;
+  // The page pass is a programmatic dependent of whatever precedes it in the stream (a no-op
+  // unless that kernel triggers early, as the split combine of a previous call does): its
+  // CTAs load their code tables while that kernel finishes.
+  {
+    cudaLaunchConfig_t mc = {};
+    mc.gridDim = dim3(grid);
+    mc.blockDim = dim3(kThreads);
+    mc.dynamicSmemBytes = smem;
+    mc.stream = s;
+    cudaLaunchAttribute ma[1];
+    ma[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    ma[0].val.programmaticStreamSerializationAllowed = 1;
+    mc.attrs = ma;
+    mc.numAttrs = 1;
+    const cudaError_t e = fast ? cudaLaunchKernelEx(&mc, decode_attention_kernel<true>, P)
+                               : cudaLaunchKernelEx(&mc, decode_attention_kernel<false>, P);
+    if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_decode_attention: ") + cudaGetErrorString(e));
+  }
   // Split combine as a programmatic dependent launch of the attention grid.
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(hkv * P.nqc * P.gmax);
