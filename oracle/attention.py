@@ -75,3 +75,37 @@ def attention_dense_tail(q, pages: dict | None, fmt: dict, tail_k, tail_v, actua
         parts_k.append(np.asarray(tail_k, np.float64))
         parts_v.append(np.asarray(tail_v, np.float64))
     return attention(q, np.concatenate(parts_k, axis=1), np.concatenate(parts_v, axis=1), actual_seq_len, scale)
+
+
+def partial(q, k, v, scale: float) -> np.ndarray:
+    """Unnormalised softmax partial of ``q (H_q,128)`` over one token range ``k, v (H_kv,T,128)``:
+    ``[H_q, 130]`` records ``(m, l, o[128])`` with ``m`` the maximum score in base-2 units,
+    ``l = sum 2^(s - m)`` and ``o = sum 2^(s - m) v`` (``s`` = score in base-2 units).
+
+    No reference counterpart (the reference runs on one device): this is the record the
+    sequence-sharded path exchanges between GPUs; an empty range gives ``m = -inf``.
+    """
+    q = np.asarray(q, np.float64)
+    hq = q.shape[0]
+    if np.asarray(k).shape[1] == 0:
+        rec = np.zeros((hq, 130))
+        rec[:, 0] = -np.inf
+        return rec
+    s = fused_scores(q, k, scale) / np.log(2.0)
+    m = s.max(axis=-1, keepdims=True)
+    w = np.exp2(s - m)
+    g = hq // np.asarray(v).shape[0]
+    vv = np.repeat(np.asarray(v, np.float64), g, axis=0)
+    return np.concatenate([m, w.sum(axis=-1, keepdims=True), np.einsum("ht,htd->hd", w, vv)], axis=-1)
+
+
+def combine(partials: np.ndarray) -> np.ndarray:
+    """Merge ``[n, H_q, 130]`` partials (log-sum-exp): ``M = max m_r``, ``L = sum l_r 2^(m_r-M)``,
+    ``O = sum o_r 2^(m_r-M) / L``; float64 ``(H_q, 128)``."""
+    p = np.asarray(partials, np.float64)
+    m = p[..., 0]
+    M = m.max(axis=0)
+    w = np.where(np.isneginf(m), 0.0, np.exp2(m - M))
+    L = (p[..., 1] * w).sum(axis=0)
+    O = (p[..., 2:] * w[..., None]).sum(axis=0)
+    return O / L[:, None]
