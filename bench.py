@@ -17,10 +17,11 @@ Reported (one JSON line on rank 0):
                measured HBM copy bandwidth
   cpu_baseline -- the NumPy oracle (the reference's CPU-fallback math) on a bounded sample
 
-Multi-GPU (torchrun, N>1): the 32K context of every layer is split into contiguous page
-ranges, one per rank (the last rank also holds the tail and the new tokens); each rank emits a
-per-head partial (max, sum, output) and one NCCL all-gather per layer feeds a log-sum-exp
-combine.  Total work is fixed, so scaling is "strong".
+Multi-GPU (torchrun, N>1): one sequence of N x 32K tokens per layer, split into contiguous
+page ranges, one 32K range per rank (the last rank also holds the tail and the new tokens);
+every rank's attention launch publishes its per-query-head partial (max, sum, output) into
+every rank's buffer over NVLink and merges them (log-sum-exp) in the same launch.  Per-GPU work
+is fixed, so scaling is "weak" (``--scaling strong --ctx C`` splits one C-token context).
 
 ``--impl reference`` times the oracle port of the reference's CPU fallback instead.
 """
@@ -174,18 +175,23 @@ def cpu_baseline(seconds_target: float = 15.0, ctx: int = CTX):
             "ms_per_layer_call": dt * 1e3}
 
 
+def _total_ctx(args, world: int) -> int:
+    return args.ctx * world if args.scaling == "weak" else args.ctx
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    cb = cpu_baseline(seconds_target=max(3.0, min(20.0, 2.0 * (args.steps + args.warmup))))
+    ctx = _total_ctx(args, int(os.environ.get("WORLD_SIZE", "1")))
+    cb = cpu_baseline(seconds_target=max(3.0, min(20.0, 2.0 * (args.steps + args.warmup))), ctx=ctx)
     step_s = cb["ms_per_layer_call"] * 1e-3 * LAYERS
     line = {
         "metric": "decode-attention HBM GB/s (% of B200 peak) and decode tokens/s at 32K ctx",
         "value": cb["value"], "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
         "dtype": "f16", "data": "synthetic", "impl": "reference",
-        "config": {"workload": "llama3-8b-attention-32layers-32k-decode", "ctx": CTX, "layers": LAYERS,
+        "config": {"workload": "llama3-8b-attention-32layers-32k-decode", "ctx": ctx, "layers": LAYERS,
                    "num_q_heads": HQ, "num_kv_heads": HKV, "head_dim": D, "batch": 1},
         "decode_tokens_per_s": 1.0 / step_s,
         "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
@@ -213,6 +219,7 @@ def run_gpu(args):
     build.build()
     cfg = TurboPolarConfig(num_q_heads=HQ, num_kv_heads=HKV)
     total_steps = args.steps + args.warmup + 2
+    CTX = _total_ctx(args, world)
     n_pages_total = CTX // PAGE
     lo, hi = sharded.page_range(n_pages_total, rank, world)
     last = rank == world - 1
@@ -222,11 +229,11 @@ def run_gpu(args):
     layers = []
     for layer in range(LAYERS):
         rt = TurboPolarKVCacheRuntime(cfg, max_seq_len=cap_tokens, check_finite=False, first_page=lo)
-        # Every rank draws the full layer so the shards are slices of one sequence.
-        gen.manual_seed(1000 + layer)
-        k = (torch.randn((1, HKV, CTX, D), generator=gen, device=dev) * chan).half()
-        v = torch.randn((1, HKV, CTX, D), generator=gen, device=dev).half()
-        rt.append(k[:, :, lo * PAGE:hi * PAGE].contiguous(), v[:, :, lo * PAGE:hi * PAGE].contiguous())
+        # Each rank draws its own slice of the layer's sequence.
+        gen.manual_seed(1000 + 64 * layer + rank)
+        k = (torch.randn((1, HKV, (hi - lo) * PAGE, D), generator=gen, device=dev) * chan).half()
+        v = torch.randn((1, HKV, (hi - lo) * PAGE, D), generator=gen, device=dev).half()
+        rt.append(k, v)
         if world > 1:
             rt.set_global_length(CTX)
         del k, v
@@ -351,9 +358,10 @@ def run_gpu(args):
         line = {
             "metric": "decode-attention HBM GB/s (% of B200 peak) and decode tokens/s at 32K ctx",
             "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
             "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "llama3-8b-attention-32layers-32k-decode", "ctx": CTX, "layers": LAYERS,
+            "config": {"workload": "llama3-8b-attention-32layers-32k-decode", "ctx": CTX,
+                       "ctx_per_gpu": CTX // world, "layers": LAYERS,
                        "num_q_heads": HQ, "num_kv_heads": HKV, "head_dim": D, "batch": 1,
                        "format": "fp16 radii, 4-bit angles (split 64), int8 V group 32",
                        "parallelism": f"sequence-shard x{world}" if world > 1 else "single GPU",
@@ -381,6 +389,8 @@ def main():
     ap.add_argument("--impl", default="turbopolar", choices=["turbopolar", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--ctx", type=int, default=CTX, help="context per GPU (weak) or in total (strong)")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

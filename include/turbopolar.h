@@ -184,6 +184,42 @@ int tp_decode_attention_noalloc(const tp_page_pool* pool, const tp_tail* tail, t
 int tp_combine_partials(const float* partials, int32_t n_parts, int32_t num_q_heads, void* out,
                         void* stream);
 
+/* ---- Sequence sharding over the GPUs of one node, merged inside the attention launch.
+ * No reference counterpart (the reference runs on one device).  Every rank holds a contiguous
+ * page range of every KV head; its attention launch publishes each query head's partial
+ * (m, l, o) into every rank's exchange buffer with peer stores over NVLink, raises a flag
+ * there, waits (bounded, about a second) for all ranks' records of that head and merges them,
+ * so each rank writes the whole fp16 output with no collective library call.  All ranks must
+ * make the same sequence of sharded calls on their buffers (the buffers' epoch words advance
+ * once per call).  A wait that runs out leaves workspace word 0 = 3 (the output is unusable). */
+#define TP_MAX_RANKS 8
+
+typedef struct tp_exchange {
+  int32_t world, rank;            /* 2 <= world <= TP_MAX_RANKS */
+  void* buffers[TP_MAX_RANKS];    /* rank r's exchange buffer as mapped in this process */
+} tp_exchange;
+
+/* Bytes of one rank's exchange buffer for `world` ranks and H_q query heads. */
+size_t tp_exchange_bytes(int32_t world, int32_t num_q_heads);
+
+/* Device memory another process can map: cudaMalloc'd, zeroed, with its 64-byte IPC handle
+ * written to handle_out (tp_ipc_open maps it in a peer process). */
+int tp_ipc_alloc(size_t bytes, void** ptr, void* handle_out);
+int tp_ipc_open(const void* handle, void** ptr);
+int tp_ipc_close(void* ptr);
+int tp_ipc_free(void* ptr);
+
+/* tp_decode_attention / tp_decode_step of one shard, merged across the ranks of `x` into
+ * `out` (no partial output). */
+int tp_decode_attention_sharded(const tp_page_pool* pool, const tp_tail* tail, tp_state state,
+                                const int32_t* d_state, const void* q, int32_t q_dtype,
+                                int32_t num_q_heads, float scale, void* out, const tp_exchange* x,
+                                void* workspace, size_t workspace_bytes, void* stream);
+int tp_decode_step_sharded(const tp_page_pool* pool, const tp_tail* tail, int32_t* d_state,
+                           const void* k_new, const void* v_new, int32_t kv_dtype, int64_t head_stride,
+                           const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
+                           const tp_exchange* x, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Scores only: scores[hq][p*64 + l] = scale * q[hq] . K[hq / G][page p][l] for local pages
  * [0, n_pages), fp16 [H_q][n_pages*64].  Replaces MetalKernelBridge.execute_fused_qk
  * (rfsn_v11/kernels/turbo_polar/metal.py:494-530, tqpolar_fused_qk.metal:4-100); accumulates

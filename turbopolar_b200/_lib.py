@@ -22,7 +22,10 @@ EXPORTED = (
     "tp_row_bytes", "tp_encode_pages", "tp_append", "tp_decode_attention_workspace_size",
     "tp_decode_attention", "tp_decode_step", "tp_decode_attention_noalloc", "tp_combine_partials", "tp_fused_scores", "tp_decode_pages",
     "tp_export_pages", "tp_import_pages", "tp_last_error", "tp_version",
+    "tp_exchange_bytes", "tp_ipc_alloc", "tp_ipc_open", "tp_ipc_close", "tp_ipc_free",
+    "tp_decode_attention_sharded", "tp_decode_step_sharded",
 )
+MAX_RANKS = 8
 
 
 class Format(ctypes.Structure):
@@ -47,6 +50,10 @@ class State(ctypes.Structure):
                 ("seq_len", ctypes.c_int32), ("first_page", ctypes.c_int32)]
 
 
+class Exchange(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("buffers", ctypes.c_void_p * 8)]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -69,6 +76,15 @@ def _declare(lib):
         "tp_decode_pages": (ctypes.c_int, [ctypes.POINTER(PagePool), I32, I32, P, P, P]),
         "tp_export_pages": (ctypes.c_int, [ctypes.POINTER(PagePool), I32, I32, ctypes.POINTER(PagePool), P]),
         "tp_import_pages": (ctypes.c_int, [ctypes.POINTER(PagePool), I32, I32, ctypes.POINTER(PagePool), P]),
+        "tp_exchange_bytes": (SZ, [I32, I32]),
+        "tp_ipc_alloc": (ctypes.c_int, [SZ, ctypes.POINTER(ctypes.c_void_p), P]),
+        "tp_ipc_open": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_void_p)]),
+        "tp_ipc_close": (ctypes.c_int, [P]),
+        "tp_ipc_free": (ctypes.c_int, [P]),
+        "tp_decode_attention_sharded": (ctypes.c_int, [ctypes.POINTER(PagePool), ctypes.POINTER(Tail), State, P, P,
+                                                       I32, I32, F, P, ctypes.POINTER(Exchange), P, SZ, P]),
+        "tp_decode_step_sharded": (ctypes.c_int, [ctypes.POINTER(PagePool), ctypes.POINTER(Tail), P, P, P, I32, I64, P,
+                                                  I32, I32, F, P, ctypes.POINTER(Exchange), P, SZ, P]),
         "tp_last_error": (ctypes.c_char_p, []),
         "tp_version": (ctypes.c_int, []),
     }

@@ -31,6 +31,7 @@
 // merges them in parallel and writes the fp16 output, then resets the ticket, all in the same
 // launch.
 #include <cfloat>
+#include <cstring>
 #include <cmath>
 #include <mutex>
 
@@ -43,6 +44,7 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kMaxHeads = 8;  // query heads per unit (N of the mma)
 constexpr int kHalf = 32;     // tokens per unit
 constexpr int kPartialStride = kMaxHeads * TP_PARTIAL_FLOATS;  // floats per workspace slot
+constexpr int kRecFloats = 132;  // (m, l, o[128]) padded to 16 bytes: exchange records
 constexpr int kLutEntries = 256;
 constexpr int kMaxContrib = 192;  // CTAs that can share one head (grid <= kMaxContrib)
 
@@ -72,6 +74,10 @@ struct AttnParams {
   const void* v_new;
   int64_t new_head_stride;
   PoolArgs wpool;
+  // Cross-GPU exchange (sequence sharding): xworld ranks; xbuf[r] is rank r's exchange buffer
+  // mapped into this process; xworld == 0 without an exchange.
+  int xworld, xrank;
+  uint8_t* xbuf[TP_MAX_RANKS];
   float scale_log2;
   __half* out;
   float* partial_out;
@@ -810,6 +816,76 @@ __device__ __noinline__ float3 flush_partial(const AttnParams& P, CombineSmem& s
   return make_float3(M, L, O);
 }
 
+// ----------------------------------------------------------------------------- cross-GPU exchange
+// Exchange buffer of one rank: records [world][H_q][kRecFloats] written by every rank into
+// every rank's buffer (peer stores over NVLink), flags [world][H_q] (the epoch of the record a
+// rank last published there), then this rank's epoch word and ticket.
+__host__ __device__ inline size_t x_flags_off(int world, int hq) {
+  return (size_t(world) * hq * kRecFloats * sizeof(float) + 255) & ~size_t(255);
+}
+__host__ __device__ inline size_t x_epoch_off(int world, int hq) {
+  return (x_flags_off(world, hq) + size_t(world) * hq * sizeof(int) + 255) & ~size_t(255);
+}
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Publish this rank's merged (m, l, o) of query head qh to every rank, wait (bounded) until
+// every rank's record of qh for this epoch is here, and merge them.  Threads d < 128 hold
+// channel d.  False after a wait ran out (a rank that never published).
+__device__ __forceinline__ bool exchange_merge(const AttnParams& P, int qh, int epoch, float& M, float& L, float& O) {
+  const int tid = threadIdx.x;
+  const int W = P.xworld, hq = P.num_q_heads;
+  for (int r = 0; r < W; ++r) {
+    float* rec = reinterpret_cast<float*>(P.xbuf[r]) + (size_t(P.xrank) * hq + qh) * kRecFloats;
+    if (tid < kD) rec[2 + tid] = O;
+    if (tid == 0) { rec[0] = M; rec[1] = L; }
+  }
+  // The barrier orders every thread's record stores before the flag stores, which release
+  // them at system scope (the peers read them over NVLink).
+  __syncthreads();
+  if (tid < W) st_release_sys(reinterpret_cast<int*>(P.xbuf[tid] + x_flags_off(W, hq)) + P.xrank * hq + qh, epoch);
+  __shared__ int s_ok;
+  if (tid == 0) s_ok = 1;
+  __syncthreads();
+  if (tid < W) {
+    const int* f = reinterpret_cast<const int*>(P.xbuf[P.xrank] + x_flags_off(W, hq)) + tid * hq + qh;
+    const long long t0 = clock64();
+    while (ld_acquire_sys(f) != epoch) {
+      if (clock64() - t0 > (1ll << 31)) {
+        s_ok = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid < kD) {
+    const float* base = reinterpret_cast<const float*>(P.xbuf[P.xrank]) + size_t(qh) * kRecFloats;
+    float Mx = -INFINITY;
+    for (int r = 0; r < W; ++r) Mx = fmaxf(Mx, __ldcv(base + size_t(r) * hq * kRecFloats));
+    float Lx = 0.f, Ox = 0.f;
+    if (Mx != -INFINITY) {
+      for (int r = 0; r < W; ++r) {
+        const float* rec = base + size_t(r) * hq * kRecFloats;
+        const float m = __ldcv(rec);
+        const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - Mx);
+        Lx = fmaf(__ldcv(rec + 1), w, Lx);
+        Ox = fmaf(__ldcv(rec + 2 + tid), w, Ox);
+      }
+    }
+    M = Mx;
+    L = Lx;
+    O = Ox;
+  }
+  return s_ok != 0;
+}
+
 // Fused step: advance the state words once every CTA has read them (ticket) and the page pass
 // has completed (griddepcontrol.wait), then reset the ticket.
 __device__ __forceinline__ void advance_state(const AttnParams& P, const tp_state& st, int n_pages, int tail_len,
@@ -828,7 +904,7 @@ __global__ void __launch_bounds__(kCombineThreads, 4) split_combine_kernel(const
   __shared__ int soff[kMaxContrib];
   __shared__ __align__(16) float s_o[kCombineWarps * kD];
   __shared__ float s_sc[kPage + kCombineWarps];
-  __shared__ int s_last;
+  __shared__ int s_last, s_epoch;
   const int tid = threadIdx.x;
   const int vh = blockIdx.x / P.gmax, h = blockIdx.x % P.gmax;
   const int kvh = vh / P.nqc, chunk = vh % P.nqc;
@@ -850,6 +926,17 @@ __global__ void __launch_bounds__(kCombineThreads, 4) split_combine_kernel(const
     }
     s_st = st;
     s_last = 0;
+    if (P.xworld > 1) {
+      // Exchange epoch: read by every CTA, advanced by the last to have read it.
+      int* ew = reinterpret_cast<int*>(P.xbuf[P.xrank] + x_epoch_off(P.xworld, P.num_q_heads));
+      const int e = ew[0] + 1;
+      s_epoch = e;
+      __threadfence();
+      if (atomicAdd(&ew[1], 1) == int(gridDim.x) - 1) {
+        ew[0] = e;
+        ew[1] = 0;
+      }
+    }
     if (P.fused) {
       __threadfence();  // the reads above happen before the ticket
       s_last = atomicAdd(&P.d_state[5], 1) == int(gridDim.x) - 1;
@@ -944,6 +1031,9 @@ __global__ void __launch_bounds__(kCombineThreads, 4) split_combine_kernel(const
       __syncthreads();
     }
   }
+  if (P.xworld > 1) {
+    if (!exchange_merge(P, qh, s_epoch, M, L, O) && tid == 0) atomicExch(P.ws_error, 3);  // a rank missing
+  }
   if (tid < kD) write_result(P, qh, tid, M, L, O);
   if (s_last && tid == 0) advance_state(P, st, n_pages, tail_len, appended, flush);
 }
@@ -1024,7 +1114,7 @@ struct StepArgs {
 static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state state, int32_t* d_state,
                          const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
                          float* partial_out, void* workspace, size_t workspace_bytes, void* stream,
-                         const StepArgs* step) {
+                         const StepArgs* step, const tp_exchange* x = nullptr) {
   Layout L;
   int st = validate_pool(pool, &L);
   if (st != TP_OK) return st;
@@ -1093,6 +1183,21 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
   P.v_new = step ? step->v_new : nullptr;
   P.new_head_stride = step ? step->head_stride : 0;
   P.wpool = pool_args(*pool, L);
+  P.xworld = 0;
+  P.xrank = 0;
+  for (int r = 0; r < TP_MAX_RANKS; ++r) P.xbuf[r] = nullptr;
+  if (x) {
+    if (x->world < 2 || x->world > TP_MAX_RANKS || x->rank < 0 || x->rank >= x->world)
+      return fail(TP_ERR_INVALID, "exchange: world must be in [2, 8] and rank in [0, world)");
+    if (!out || partial_out) return fail(TP_ERR_INVALID, "exchange: a sharded call writes `out` only");
+    for (int r = 0; r < x->world; ++r) {
+      if (!x->buffers[r] || (reinterpret_cast<uintptr_t>(x->buffers[r]) & 255))
+        return fail(TP_ERR_INVALID, "exchange: every rank's buffer must be mapped and 256-byte aligned");
+      P.xbuf[r] = static_cast<uint8_t*>(x->buffers[r]);
+    }
+    P.xworld = x->world;
+    P.xrank = x->rank;
+  }
   P.ws_partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
   // Half-page stage: radii | v codes | level-1 codes | 64-byte bank shift | deep codes | v scales.
   auto up = [](int x, int a) { return (x + a - 1) / a * a; };
@@ -1162,6 +1267,20 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
   return TP_OK;
 }
 
+static int check_step_args(const tp_page_pool* pool, const tp_tail* tail, const int32_t* d_state, const void* k_new,
+                           const void* v_new, int32_t kv_dtype, int64_t head_stride) {
+  if (!d_state) return fail(TP_ERR_INVALID, "tp_decode_step: the state words are required");
+  if (!pool || !tail) return fail(TP_ERR_INVALID, "tp_decode_step: NULL pool or tail");
+  if (!k_new || !v_new) return fail(TP_ERR_INVALID, "tp_decode_step: NULL new token");
+  if (kv_dtype != tail->dtype) return fail(TP_ERR_INVALID, "tp_decode_step: new token dtype must match the tail");
+  if (kv_dtype != TP_F16 && kv_dtype != TP_F32) return fail(TP_ERR_INVALID, "only float16 and float32 inputs are supported");
+  const int64_t esz = kv_dtype == TP_F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(k_new) & 15) || (reinterpret_cast<uintptr_t>(v_new) & 15) ||
+      head_stride < kD || (head_stride * esz) % 16)
+    return fail(TP_ERR_INVALID, "tp_decode_step: new token rows must be 16-byte aligned, heads >= 128 elements apart");
+  return TP_OK;
+}
+
 int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state state, const int32_t* d_state,
                         const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
                         float* partial_out, void* workspace, size_t workspace_bytes, void* stream) {
@@ -1174,19 +1293,76 @@ int tp_decode_step(const tp_page_pool* pool, const tp_tail* tail, int32_t* d_sta
                    const void* v_new, int32_t kv_dtype, int64_t head_stride, const void* q, int32_t q_dtype,
                    int32_t num_q_heads, float scale, void* out, float* partial_out, void* workspace,
                    size_t workspace_bytes, void* stream) {
-  if (!d_state) return fail(TP_ERR_INVALID, "tp_decode_step: the state words are required");
-  if (!pool || !tail) return fail(TP_ERR_INVALID, "tp_decode_step: NULL pool or tail");
-  if (!k_new || !v_new) return fail(TP_ERR_INVALID, "tp_decode_step: NULL new token");
-  if (kv_dtype != tail->dtype) return fail(TP_ERR_INVALID, "tp_decode_step: new token dtype must match the tail");
-  if (kv_dtype != TP_F16 && kv_dtype != TP_F32) return fail(TP_ERR_INVALID, "only float16 and float32 inputs are supported");
-  const int64_t esz = kv_dtype == TP_F32 ? 4 : 2;
-  if ((reinterpret_cast<uintptr_t>(k_new) & 15) || (reinterpret_cast<uintptr_t>(v_new) & 15) ||
-      head_stride < kD || (head_stride * esz) % 16)
-    return fail(TP_ERR_INVALID, "tp_decode_step: new token rows must be 16-byte aligned, heads >= 128 elements apart");
+  const int st = check_step_args(pool, tail, d_state, k_new, v_new, kv_dtype, head_stride);
+  if (st != TP_OK) return st;
   StepArgs a{k_new, v_new, head_stride};
   tp_state none = {0, 0, 0, 0};
   return run_attention(pool, tail, none, d_state, q, q_dtype, num_q_heads, scale, out, partial_out, workspace,
                        workspace_bytes, stream, &a);
+}
+
+size_t tp_exchange_bytes(int32_t world, int32_t num_q_heads) {
+  if (world < 2 || world > TP_MAX_RANKS || num_q_heads <= 0) return 0;
+  return x_epoch_off(world, num_q_heads) + 256;
+}
+
+int tp_ipc_alloc(size_t bytes, void** ptr, void* handle_out) {
+  if (!ptr || !handle_out || bytes == 0) return fail(TP_ERR_INVALID, "tp_ipc_alloc: bad arguments");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    return fail(TP_ERR_CUDA, std::string("tp_ipc_alloc: ") + cudaGetErrorString(e));
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handles are 64 bytes");
+  std::memcpy(handle_out, &h, sizeof(h));
+  *ptr = p;
+  return TP_OK;
+}
+
+int tp_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return fail(TP_ERR_INVALID, "tp_ipc_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_ipc_open: ") + cudaGetErrorString(e));
+  return TP_OK;
+}
+
+int tp_ipc_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_ipc_close: ") + cudaGetErrorString(e));
+  return TP_OK;
+}
+
+int tp_ipc_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_ipc_free: ") + cudaGetErrorString(e));
+  return TP_OK;
+}
+
+int tp_decode_attention_sharded(const tp_page_pool* pool, const tp_tail* tail, tp_state state, const int32_t* d_state,
+                                const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
+                                const tp_exchange* x, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x) return fail(TP_ERR_INVALID, "tp_decode_attention_sharded: exchange is NULL");
+  return run_attention(pool, tail, state, const_cast<int32_t*>(d_state), q, q_dtype, num_q_heads, scale, out,
+                       nullptr, workspace, workspace_bytes, stream, nullptr, x);
+}
+
+int tp_decode_step_sharded(const tp_page_pool* pool, const tp_tail* tail, int32_t* d_state, const void* k_new,
+                           const void* v_new, int32_t kv_dtype, int64_t head_stride, const void* q, int32_t q_dtype,
+                           int32_t num_q_heads, float scale, void* out, const tp_exchange* x, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (!x) return fail(TP_ERR_INVALID, "tp_decode_step_sharded: exchange is NULL");
+  const int st = check_step_args(pool, tail, d_state, k_new, v_new, kv_dtype, head_stride);
+  if (st != TP_OK) return st;
+  StepArgs a{k_new, v_new, head_stride};
+  tp_state none = {0, 0, 0, 0};
+  return run_attention(pool, tail, none, d_state, q, q_dtype, num_q_heads, scale, out, nullptr, workspace,
+                       workspace_bytes, stream, &a, x);
 }
 
 // ----------------------------------------------------------------------------- no-allocation variant

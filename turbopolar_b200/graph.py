@@ -32,10 +32,18 @@ def launch_append(rt: TurboPolarKVCacheRuntime, k: torch.Tensor, v: torch.Tensor
 
 
 def launch_attention(rt: TurboPolarKVCacheRuntime, q: torch.Tensor, out: Optional[torch.Tensor], scale: float,
-                     partial_out: Optional[torch.Tensor] = None) -> None:
-    """Enqueue tp_decode_attention reading the device counters."""
+                     partial_out: Optional[torch.Tensor] = None, exchange=None) -> None:
+    """Enqueue tp_decode_attention reading the device counters (tp_decode_attention_sharded
+    with an ``exchange``: merged across ranks into ``out``)."""
     B, Hq = q.shape[0], q.shape[-2]
     ws = rt._workspace_for(B * Hq)
+    if exchange is not None:
+        _lib.check(_lib.lib().tp_decode_attention_sharded(
+            ctypes.byref(rt.pool_struct()), ctypes.byref(rt.tail_struct()), rt.state(), rt.d_state.data_ptr(),
+            q.data_ptr(), _lib.TP_F16 if q.dtype == torch.float16 else _lib.TP_F32, B * Hq, float(scale),
+            out.data_ptr(), ctypes.byref(exchange.struct), ws.data_ptr(), ws.numel(),
+            torch.cuda.current_stream(q.device).cuda_stream))
+        return
     _lib.check(_lib.lib().tp_decode_attention(
         ctypes.byref(rt.pool_struct()), ctypes.byref(rt.tail_struct()), rt.state(), rt.d_state.data_ptr(),
         q.data_ptr(), _lib.TP_F16 if q.dtype == torch.float16 else _lib.TP_F32, B * Hq, float(scale),
@@ -44,9 +52,10 @@ def launch_attention(rt: TurboPolarKVCacheRuntime, q: torch.Tensor, out: Optiona
 
 
 def launch_decode_step(rt: TurboPolarKVCacheRuntime, k: torch.Tensor, v: torch.Tensor, q: torch.Tensor,
-                       out: Optional[torch.Tensor], scale: float, partial_out: Optional[torch.Tensor] = None) -> None:
+                       out: Optional[torch.Tensor], scale: float, partial_out: Optional[torch.Tensor] = None,
+                       exchange=None) -> None:
     """Enqueue tp_decode_step (append one token ``(B, H_kv, 1, 128)``, then attend) on the
-    device counters."""
+    device counters (tp_decode_step_sharded with an ``exchange``)."""
     B, H, T, D = k.shape
     kf = k.reshape(B * H, D)
     vf = v.reshape(B * H, D)
@@ -54,6 +63,14 @@ def launch_decode_step(rt: TurboPolarKVCacheRuntime, k: torch.Tensor, v: torch.T
         raise ValueError("new K and V rows must share one layout with contiguous channels")
     Bq, Hq = q.shape[0], q.shape[-2]
     ws = rt._workspace_for(Bq * Hq)
+    kvd = _lib.TP_F16 if k.dtype == torch.float16 else _lib.TP_F32
+    qd = _lib.TP_F16 if q.dtype == torch.float16 else _lib.TP_F32
+    if exchange is not None:
+        _lib.check(_lib.lib().tp_decode_step_sharded(
+            ctypes.byref(rt.pool_struct()), ctypes.byref(rt.tail_struct()), rt.d_state.data_ptr(), kf.data_ptr(),
+            vf.data_ptr(), kvd, kf.stride(0), q.data_ptr(), qd, Bq * Hq, float(scale), out.data_ptr(),
+            ctypes.byref(exchange.struct), ws.data_ptr(), ws.numel(), torch.cuda.current_stream(q.device).cuda_stream))
+        return
     _lib.check(_lib.lib().tp_decode_step(
         ctypes.byref(rt.pool_struct()), ctypes.byref(rt.tail_struct()), rt.d_state.data_ptr(), kf.data_ptr(),
         vf.data_ptr(), _lib.TP_F16 if k.dtype == torch.float16 else _lib.TP_F32, kf.stride(0), q.data_ptr(),

@@ -1,12 +1,16 @@
-"""Sequence-sharded decode attention over several GPUs (one process per GPU).
+"""Sequence-sharded decode attention over the GPUs of one node (one process per GPU).
 
 The reference is single-device (no collective exists in it).  For contexts too long for one
 GPU's bandwidth, the pages of every KV head are split into contiguous ranges, one per rank;
 the last rank also holds the dense tail and receives the new tokens.  Each rank computes, for
-every query head, an unnormalised partial (m in log2 units, l, o[128]) over its range
-(``tp_decode_attention`` with ``partial_out``), one NCCL all-gather per layer exchanges the
-``H_q x 130`` floats, and every rank merges them with ``tp_combine_partials``:
-``M = max m_r, L = sum l_r 2^(m_r-M), O = sum o_r 2^(m_r-M) / L``.
+every query head, an unnormalised partial (m in log2 units, l, o[128]) over its range, and the
+partials are merged with ``M = max m_r, L = sum l_r 2^(m_r-M), O = sum o_r 2^(m_r-M) / L``.
+
+Two exchanges: ``PeerExchange`` (the default) does it inside the attention launch -- every
+rank's split-combine CTAs store their records into every rank's buffer over NVLink (buffers
+mapped through CUDA IPC), raise a flag, wait (bounded) for the other ranks' records and merge;
+the NCCL path (``exchange=False``) writes ``partial_out``, all-gathers it and runs
+``tp_combine_partials``.
 """
 
 from __future__ import annotations
@@ -51,33 +55,106 @@ def sharded_attention(rt: TurboPolarKVCacheRuntime, q: torch.Tensor, group=None)
     return combine(gathered, out)
 
 
+class PeerExchange:
+    """This rank's exchange buffer and every other rank's, mapped into this process through
+    CUDA IPC (handles all-gathered over ``group``).  One per call site that is replayed in
+    step: every rank must make the same sequence of sharded calls on it."""
+
+    def __init__(self, num_q_heads: int, group=None):
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not 2 <= self.world <= _lib.MAX_RANKS:
+            raise ValueError(f"peer exchange needs 2..{_lib.MAX_RANKS} ranks, got {self.world}")
+        lib = _lib.lib()
+        nbytes = lib.tp_exchange_bytes(self.world, num_q_heads)
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        _lib.check(lib.tp_ipc_alloc(nbytes, ctypes.byref(own), handle))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._own = own.value
+        self._opened = []
+        bufs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                bufs.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            hb = (ctypes.c_ubyte * 64).from_buffer_copy(h)
+            _lib.check(lib.tp_ipc_open(hb, ctypes.byref(p)))
+            self._opened.append(p.value)
+            bufs.append(p.value)
+        arr = (ctypes.c_void_p * _lib.MAX_RANKS)(*(bufs + [None] * (_lib.MAX_RANKS - self.world)))
+        self.struct = _lib.Exchange(self.world, self.rank, arr)
+        self._group = group
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this one (collective: peers may still write into it
+        until every rank is past its last call)."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self._group)
+        lib = _lib.lib()
+        for p in self._opened:
+            lib.tp_ipc_close(p)
+        dist.barrier(group=self._group)
+        lib.tp_ipc_free(self._own)
+        self._own = None
+
+
+def exchange_attention(rt: TurboPolarKVCacheRuntime, q: torch.Tensor, exchange: PeerExchange,
+                       out: torch.Tensor = None) -> torch.Tensor:
+    """Eager sharded attention merged inside the launch (``tp_decode_attention_sharded``)."""
+    B, Hq = q.shape[0], q.shape[-2]
+    if out is None:
+        out = torch.empty((B, Hq, 128), dtype=torch.float16, device=q.device)
+    qf = q.reshape(B * Hq, 128).contiguous()
+    ws = rt._workspace_for(B * Hq)
+    _lib.check(_lib.lib().tp_decode_attention_sharded(
+        ctypes.byref(rt.pool_struct()), ctypes.byref(rt.tail_struct()), rt.state(), None, qf.data_ptr(),
+        _lib.TP_F16 if qf.dtype == torch.float16 else _lib.TP_F32, B * Hq, float(rt.config.attention_scale),
+        out.data_ptr(), ctypes.byref(exchange.struct), ws.data_ptr(), ws.numel(),
+        torch.cuda.current_stream(q.device).cuda_stream))
+    return out
+
+
 class ShardedDecodeStep:
     """One captured decode step over all layers: local attention partial (the last rank appends
     the new token in the same call, tp_decode_step), NCCL all-gather, combine.  The graph must
     be released (``release()``) before the process group is destroyed."""
 
     def __init__(self, layers: List[TurboPolarKVCacheRuntime], k_in, v_in, q_in, out, rank: int, world: int,
-                 group=None):
+                 group=None, exchange: bool = True):
         self.layers, self.rank, self.world, self.group = layers, rank, world, group
         self.last = rank == world - 1
         dev = q_in[0].device
         hq = q_in[0].shape[0] * q_in[0].shape[-2]
         self.partials = [torch.empty((hq, _lib.PARTIAL_FLOATS), dtype=torch.float32, device=dev) for _ in layers]
-        self.gathered = [torch.empty((world, hq, _lib.PARTIAL_FLOATS), dtype=torch.float32, device=dev)
-                         for _ in layers]
         for rt, q in zip(layers, q_in):
             rt._workspace_for(hq)
-        # NCCL warm-up outside the capture.
-        dist.all_gather_into_tensor(self.gathered[0], self.partials[0], group=group)
+        self.exchanges = [PeerExchange(hq, group) for _ in layers] if exchange else None
+        if not exchange:
+            self.gathered = [torch.empty((world, hq, _lib.PARTIAL_FLOATS), dtype=torch.float32, device=dev)
+                             for _ in layers]
+            # NCCL warm-up outside the capture.
+            dist.all_gather_into_tensor(self.gathered[0], self.partials[0], group=group)
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             for i, rt in enumerate(layers):
+                s = rt.config.attention_scale
+                if exchange:
+                    x = self.exchanges[i]
+                    if self.last:
+                        graph.launch_decode_step(rt, k_in[i], v_in[i], q_in[i], out[i], s, exchange=x)
+                    else:
+                        graph.launch_attention(rt, q_in[i], out[i], s, exchange=x)
+                    continue
                 if self.last:
-                    graph.launch_decode_step(rt, k_in[i], v_in[i], q_in[i], None, rt.config.attention_scale,
-                                             partial_out=self.partials[i])
+                    graph.launch_decode_step(rt, k_in[i], v_in[i], q_in[i], None, s, partial_out=self.partials[i])
                 else:
-                    graph.launch_attention(rt, q_in[i], None, rt.config.attention_scale, partial_out=self.partials[i])
+                    graph.launch_attention(rt, q_in[i], None, s, partial_out=self.partials[i])
                 dist.all_gather_into_tensor(self.gathered[i], self.partials[i], group=group)
                 combine(self.gathered[i], out[i])
         torch.cuda.synchronize()
@@ -96,3 +173,7 @@ class ShardedDecodeStep:
     def release(self) -> None:
         torch.cuda.synchronize()
         self.graph = None
+        if self.exchanges:
+            for x in self.exchanges:
+                x.close()
+            self.exchanges = None
