@@ -43,8 +43,10 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxHeads = 8;  // query heads per unit (N of the mma)
 constexpr int kHalf = 32;     // tokens per unit
-constexpr int kPartialStride = kMaxHeads * TP_PARTIAL_FLOATS;  // floats per workspace slot
-constexpr int kRecFloats = 132;  // (m, l, o[128]) padded to 16 bytes: exchange records
+// Records exchanged between CTAs and between GPUs: (m, l, o[128]) per query head, padded to
+// 132 floats so each starts on 16 bytes (staged with 16-byte copies).
+constexpr int kRecFloats = 132;
+constexpr int kPartialStride = kMaxHeads * kRecFloats;  // floats per workspace slot
 constexpr int kLutEntries = 256;
 constexpr int kMaxContrib = 192;  // CTAs that can share one head (grid <= kMaxContrib)
 
@@ -88,16 +90,34 @@ struct AttnParams {
   uint32_t lut[2 * kLutEntries];  // half2 (cos, sin) per code: level-1 [0, 256), deep [256, 512)
 };
 
-// Work partition: CTA cc of C owns units [floor(cc*U/C), floor((cc+1)*U/C)).  U < 2^31 and
-// C <= 2^16, so every product below is exact in a double and the quotient's rounding error is
-// far below the distance to the next integer; this keeps 64-bit integer division (a long
-// inline instruction sequence) out of the kernel.
-__device__ __forceinline__ int part_begin(int cc, int C, int U) {
-  return int(floor(double(cc) * double(U) / double(C)));
+// Work partition: the U units (half pages, head-major, uph per head) are cut into C = min(U,
+// grid) ranges; CTA cc owns [floor(cc*U/C), floor((cc+1)*U/C)).  With U = k*C + r,
+// floor(cc*U/C) = cc*k + floor(cc*r/C) and cc*r < C^2 fits in 32 bits, so the device does
+// neither 64-bit nor floating-point division (both are long or slow instruction sequences).
+struct Grid {
+  int uph, U, C, k, r;
+};
+
+__device__ __forceinline__ Grid grid_of(int num_vh, int n_pages, int grid) {
+  Grid g;
+  g.uph = 2 * n_pages;
+  g.U = num_vh * g.uph;
+  g.C = g.U < grid ? g.U : grid;
+  g.k = g.C > 0 ? g.U / g.C : 0;
+  g.r = g.C > 0 ? g.U - g.k * g.C : 0;
+  return g;
 }
-// The CTA whose range holds unit u.
-__device__ __forceinline__ int part_owner(int u, int C, int U) {
-  return int(floor((double(u + 1) * double(C) - 1.0) / double(U)));
+
+__device__ __forceinline__ int part_begin(const Grid& g, int cc) { return cc * g.k + (cc * g.r) / g.C; }
+
+// The CTA whose range holds unit u (0 <= u < U): a float estimate, exact within one, then
+// corrected against part_begin.
+__device__ __forceinline__ int part_owner(const Grid& g, int u) {
+  int c = int(float(u) * float(g.C) / float(g.U));
+  c = min(max(c, 0), g.C - 1);
+  while (c + 1 < g.C && part_begin(g, c + 1) <= u) ++c;
+  while (c > 0 && part_begin(g, c) > u) --c;
+  return c;
 }
 
 __device__ __forceinline__ int64_t clamp64(int64_t x, int64_t lo, int64_t hi) { return x < lo ? lo : (x > hi ? hi : x); }
@@ -413,12 +433,11 @@ struct Part {
 __device__ __forceinline__ Part make_part(const AttnParams& P, const tp_state& st, int c, int warp) {
   Part pt = {};
   pt.n_pages = min(max(st.n_pages, 0), P.page_capacity);
-  const int uph = 2 * pt.n_pages;
-  const int U = P.num_kv_heads * P.nqc * uph;
-  const int C = U < int(gridDim.x) ? U : int(gridDim.x);
-  pt.active = U > 0 && c < C;
+  const Grid g = grid_of(P.num_kv_heads * P.nqc, pt.n_pages, int(gridDim.x));
+  const int uph = g.uph;
+  pt.active = g.U > 0 && c < g.C;
   if (!pt.active) return pt;
-  const int u0 = part_begin(c, C, U), u1 = part_begin(c + 1, C, U);
+  const int u0 = part_begin(g, c), u1 = part_begin(g, c + 1);
   pt.vh_first = u0 / uph;
   pt.nseg = (u1 - 1) / uph - pt.vh_first + 1;
   const int hb0 = pt.vh_first * uph;
@@ -587,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
         L = fmaf(r[1], f, L);
         O = fmaf(r[2 + d], f, O);
       }
-      float* out = slot + h * TP_PARTIAL_FLOATS;
+      float* out = slot + h * kRecFloats;
       if (d == 0) { out[0] = M; out[1] = L; }
       out[2 + d] = O;
     }
@@ -714,7 +733,7 @@ struct SmemPage {
 };
 
 union CombineSmem {
-  float recs[kCombineChunk][TP_PARTIAL_FLOATS];
+  float recs[kCombineChunk][kRecFloats];
   SmemPage page;
 };
 
@@ -988,49 +1007,74 @@ __global__ void __launch_bounds__(kCombineThreads, 4) split_combine_kernel(const
   // Token dropped: 1 = tail state out of range, 2 = page pool full.
   if (P.fused && !appended && tid == 0 && designated) P.d_state[4] = tail_len >= kPage ? 1 : 2;
 
-  asm volatile("griddepcontrol.wait;\n" ::: "memory");
-  // The page pass's partition, recomputed from the same state it read.
-  const int uph = 2 * n_pages;
-  const int U = P.num_kv_heads * P.nqc * uph;
-  const int C = U < P.main_grid ? U : P.main_grid;
-  if (U > 0) {
-    const int c_lo = part_owner(vh * uph, C, U), c_hi = part_owner(vh * uph + uph - 1, C, U);
-    const int n = c_hi - c_lo + 1;
+  // The page pass's partition, recomputed from the same state it read, and the workspace
+  // offset of every record to merge: all known before the page pass completes.
+  const Grid g = grid_of(P.num_kv_heads * P.nqc, n_pages, P.main_grid);
+  int n = 0;
+  if (g.U > 0) {
+    const int c_lo = part_owner(g, vh * g.uph);
+    n = part_owner(g, vh * g.uph + g.uph - 1) - c_lo + 1;
     for (int ci = tid; ci < n; ci += kCombineThreads) {
       const int cc = c_lo + ci;
-      soff[ci] = (cc * 2 + (vh - part_begin(cc, C, U) / uph)) * kPartialStride + h * TP_PARTIAL_FLOATS;
-    }
-    __syncthreads();
-#pragma unroll 1
-    for (int c0 = 0; c0 < n; c0 += kCombineChunk) {
-      const int cn = min(kCombineChunk, n - c0);
-      for (int i = tid; i < cn * (TP_PARTIAL_FLOATS / 2); i += kCombineThreads) {
-        const int ci = i / (TP_PARTIAL_FLOATS / 2), e = 2 * (i - ci * (TP_PARTIAL_FLOATS / 2));
-        cp_async8(&sm.recs[ci][e], P.ws_partials + soff[c0 + ci] + e);
-      }
-      cp_async_commit();
-      cp_async_wait<0>();
-      __syncthreads();
-      if (tid < kD) {
-        float Mc = M;
-        for (int ci = 0; ci < cn; ++ci) Mc = fmaxf(Mc, sm.recs[ci][0]);
-        if (Mc != -INFINITY) {
-          const float a = (M == -INFINITY) ? 0.f : exp2_approx(M - Mc);
-          L *= a;
-          O *= a;
-#pragma unroll 4
-          for (int ci = 0; ci < cn; ++ci) {
-            const float m = sm.recs[ci][0];
-            const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - Mc);
-            L = fmaf(sm.recs[ci][1], w, L);
-            O = fmaf(sm.recs[ci][2 + tid], w, O);
-          }
-          M = Mc;
-        }
-      }
-      __syncthreads();
+      soff[ci] = (cc * 2 + (vh - part_begin(g, cc) / g.uph)) * kPartialStride + h * kRecFloats;
     }
   }
+  __syncthreads();
+
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  // Two threads per channel: thread t merges the records of parity t >> 7 for channel t & 127;
+  // the halves are combined at the end (the dense-tail partial starts in half 0).
+  const int d = tid & (kD - 1), half = tid >> 7;
+  float Mh = half ? -INFINITY : M, Lh = half ? 0.f : L, Oh = half ? 0.f : O;
+#pragma unroll 1
+  for (int c0 = 0; c0 < n; c0 += kCombineChunk) {
+    const int cn = min(kCombineChunk, n - c0);
+    constexpr int kQuads = kRecFloats / 4;
+    for (int i = tid; i < cn * kQuads; i += kCombineThreads) {
+      const int ci = i / kQuads, e = 4 * (i - ci * kQuads);
+      cp_async16(&sm.recs[ci][e], P.ws_partials + soff[c0 + ci] + e);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    float Mc = Mh;
+    for (int ci = half; ci < cn; ci += 2) Mc = fmaxf(Mc, sm.recs[ci][0]);
+    if (Mc != -INFINITY) {
+      const float a = (Mh == -INFINITY) ? 0.f : exp2_approx(Mh - Mc);
+      Lh *= a;
+      Oh *= a;
+#pragma unroll 4
+      for (int ci = half; ci < cn; ci += 2) {
+        const float m = sm.recs[ci][0];
+        const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - Mc);
+        Lh = fmaf(sm.recs[ci][1], w, Lh);
+        Oh = fmaf(sm.recs[ci][2 + d], w, Oh);
+      }
+      Mh = Mc;
+    }
+    __syncthreads();
+  }
+  if (half) {
+    s_o[d] = Mh;
+    s_o[kD + d] = Lh;
+    s_o[2 * kD + d] = Oh;
+  }
+  __syncthreads();
+  if (!half) {
+    const float m1 = s_o[d], l1 = s_o[kD + d], o1 = s_o[2 * kD + d];
+    const float Mx = fmaxf(Mh, m1);
+    if (Mx != -INFINITY) {
+      const float a0 = (Mh == -INFINITY) ? 0.f : exp2_approx(Mh - Mx);
+      const float a1 = (m1 == -INFINITY) ? 0.f : exp2_approx(m1 - Mx);
+      L = Lh * a0 + l1 * a1;
+      O = Oh * a0 + o1 * a1;
+    } else {
+      L = 0.f;
+      O = 0.f;
+    }
+    M = Mx;
+  }
+  __syncthreads();
   if (P.xworld > 1) {
     if (!exchange_merge(P, qh, s_epoch, M, L, O) && tid == 0) atomicExch(P.ws_error, 3);  // a rank missing
   }
