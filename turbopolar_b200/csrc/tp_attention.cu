@@ -615,12 +615,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
 
 // Merge the per-CTA partials of one query head -- from the CTAs whose unit ranges cover its
 // (KV head, query chunk) -- with the partial of the tokens after the pages, and write the
-// output.  One CTA per query head; thread d < 128 owns channel d of the merge.  Launched as a
+// output.  One CTA per query head; two threads per channel in the merge.  Launched as a
 // programmatic dependent of the page pass: its CTAs become resident while that grid runs (they
 // share the SM with a page-pass CTA) and compute the dense-tail partial then;
 // griddepcontrol.wait releases them once the page pass has completed and its memory is
-// visible, so no fence or atomic sits on the merge path.  Contributor records are staged in
-// shared memory by concurrent 8-byte cp.async copies (one memory round trip per 64 records).
+// visible, so no fence or atomic sits on the merge path.  The records' offsets are computed
+// before the wait; after it they are staged in shared memory by concurrent 16-byte cp.async
+// copies (one memory round trip per 64 records).
 //
 // Fused decode step (P.fused): the kernel also appends the new token of every KV head, as
 // TurboPolarKVCacheRuntime.append does before attention (turbo_polar_cache.py:106-161).
