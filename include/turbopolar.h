@@ -51,20 +51,38 @@ typedef struct tp_format {
   int32_t int8_radii; /* 0: float16 radii; 1: log-int8 radii + one float16 scale per page */
 } tp_format;
 
-/* Device page pool: one structure-of-arrays store per field, pages of one KV head contiguous,
- * with the reference's block-storage field sizes (rfsn_v11/generation/storage.py:17-169) and
- * its codes bit for bit, ordered inside each page for the decode kernel:
- *   radii            [H_kv][page_capacity][64][64]  float16 (int8 when fmt.int8_radii); float16
- *                    rows are XOR-swizzled: 16-byte chunk c of row l is stored at chunk c^(l&7)
- *   radii_scales     [H_kv][page_capacity]          float16 (fmt.int8_radii only, else NULL)
- *   angle_codes_l1   [H_kv][page_capacity][64][l1_row_bytes]   uint8, packed as the reference
- *   angle_codes_deep [H_kv][page_capacity][64][deep_row_bytes] uint8, packed as the reference
- *   v_codes          [H_kv][page_capacity][8192]    uint8 (code ^ 0x80) in mma fragment order
- *   v_scales         [H_kv][page_capacity][256]     float16 in fragment order
- * tp_export_pages / tp_import_pages convert pages to and from the reference layout
- * (radii [64][64] row-major, v_codes int8 [64][128], v_scales [64][4]).
- * Row byte counts come from tp_row_bytes().  Base pointers must be 16-byte aligned. */
+/* Device page pool in the kernels' layout: one contiguous page block per (KV head, page), made
+ * of two "units" (half pages, tokens 0-31 and 32-63), so a decode kernel streams a half page
+ * with one bulk copy.  A unit of tp_unit_bytes(fmt) bytes holds, in this order:
+ *   radii     [32][64] float16 (int8 when fmt.int8_radii); float16 rows are XOR-swizzled:
+ *             16-byte chunk c of row l is stored at chunk c ^ (l & 7)
+ *   v_codes   4096 bytes, (code ^ 0x80) in mma fragment order
+ *   codes     [32][l1_row + deep_row]: each token row holds its level-1 codes then its deep
+ *             codes, each packed exactly as the reference packs them
+ *   v_scales  [128] float16 in fragment order (one per token and 32-channel group)
+ * The codes are the reference's block-storage codes (rfsn_v11/generation/storage.py:17-169)
+ * bit for bit; only their placement differs.  tp_export_pages / tp_import_pages convert to and
+ * from the reference layout (tp_block_store).  Fields:
+ *   pages         [H_kv][page_capacity][2 * tp_unit_bytes(fmt)] bytes, 16-byte aligned
+ *   radii_scales  [H_kv][page_capacity] float16 (fmt.int8_radii only, else NULL) */
 typedef struct tp_page_pool {
+  void* pages;
+  void* radii_scales;
+  int32_t num_kv_heads;
+  int32_t page_capacity;
+  tp_format fmt;
+} tp_page_pool;
+
+/* Pages in the reference's block-storage layout (rfsn_v11/generation/storage.py:89-102 and
+ * :160-169), one array per field with every page of a head contiguous:
+ *   radii            [H_kv][page_capacity][64][64]  float16 (int8 when fmt.int8_radii), row-major
+ *   radii_scales     [H_kv][page_capacity]          float16 (fmt.int8_radii only, else NULL)
+ *   angle_codes_l1   [H_kv][page_capacity][64][l1_row_bytes]   uint8
+ *   angle_codes_deep [H_kv][page_capacity][64][deep_row_bytes] uint8
+ *   v_codes          [H_kv][page_capacity][64][128] int8
+ *   v_scales         [H_kv][page_capacity][64][4]   float16
+ * Key fields may all be NULL (values only).  Row byte counts come from tp_row_bytes(). */
+typedef struct tp_block_store {
   void* radii;
   void* radii_scales;
   void* angle_codes_l1;
@@ -74,7 +92,7 @@ typedef struct tp_page_pool {
   int32_t num_kv_heads;
   int32_t page_capacity;
   tp_format fmt;
-} tp_page_pool;
+} tp_block_store;
 
 /* Dense tail (the reference's partial block, rfsn_v11/generation/turbo_polar_cache.py:110-126):
  * k and v are [H_kv][64][128] in `dtype`, the first tail_len token rows valid. */
@@ -104,6 +122,11 @@ typedef struct tp_state {
  * (tests/benchmarks/test_turbo_polar_offline.py:26-34).  Returns TP_ERR_UNSUPPORTED for a
  * format outside turbo_polar_config.py / encoder.py's accepted bit widths. */
 int tp_row_bytes(const tp_format* fmt, int32_t* l1_row_bytes, int32_t* deep_row_bytes);
+
+/* Bytes of one unit (half page of one KV head) of a tp_page_pool in format `fmt`: the
+ * reference's block payload per 32 tokens without the radius scale (296 x 32 = 9472 for the
+ * default format; rfsn_v11/generation/turbo_polar_cache.py:154-161 counts the same bytes). */
+int tp_unit_bytes(const tp_format* fmt, int32_t* unit_bytes);
 
 /* Encode n_pages full 64-token blocks of dense keys/values into pool pages
  * [dst_page, dst_page + n_pages) of every KV head.  Token t of head h of the source is at
@@ -236,17 +259,17 @@ int tp_decode_pages(const tp_page_pool* pool, int32_t first_page, int32_t n_page
                     void* v_out, void* stream);
 
 /* Copy pages [first_page, first_page + n_pages) of `pool` into pages [0, n_pages) of `ref`,
- * a pool of the same heads and format laid out exactly as the reference stores blocks
- * (storage.py:89-102 and :160-169: radii [64][64], v_codes int8 [64][128], v_scales [64][4]),
- * e.g. to serve TurboPolarKVCacheRuntime.get_fused_attention_inputs
- * (rfsn_v11/generation/turbo_polar_cache.py:163-198). */
-int tp_export_pages(const tp_page_pool* pool, int32_t first_page, int32_t n_pages, const tp_page_pool* ref,
+ * a block store of the same heads and format (storage.py:89-102 and :160-169), e.g. to serve
+ * TurboPolarKVCacheRuntime.get_fused_attention_inputs
+ * (rfsn_v11/generation/turbo_polar_cache.py:163-198).  With ref's key fields NULL only the
+ * values are copied. */
+int tp_export_pages(const tp_page_pool* pool, int32_t first_page, int32_t n_pages, const tp_block_store* ref,
                     void* stream);
 
 /* The inverse: load reference-layout pages [0, n_pages) of `ref` into pool pages
  * [first_page, first_page + n_pages) (payloads handed to the bridge's execute_* calls,
  * rfsn_v11/kernels/turbo_polar/metal.py:651-792). */
-int tp_import_pages(const tp_page_pool* pool, int32_t first_page, int32_t n_pages, const tp_page_pool* ref,
+int tp_import_pages(const tp_page_pool* pool, int32_t first_page, int32_t n_pages, const tp_block_store* ref,
                     void* stream);
 
 /* Message of the last failed call on this thread ("" if none). */

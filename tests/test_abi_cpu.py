@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 def test_version_and_row_bytes(lib):
     from turbopolar_b200 import _lib
-    assert lib.tp_version() == 1
+    assert lib.tp_version() == 2
     cases = {  # (l1_bits, deep_bits, split_dim) -> (l1_row, deep_row); test_turbo_polar_offline.py:26-34
         (4, 4, 64): (16, 16), (4, 8, 0): (0, 64), (8, 2, 32): (16, 12), (4, 8, 128): (32, 0), (4, 2, 2): (1, 16),
     }
@@ -45,6 +45,13 @@ def test_version_and_row_bytes(lib):
         a, b = ctypes.c_int32(), ctypes.c_int32()
         assert lib.tp_row_bytes(ctypes.byref(f), ctypes.byref(a), ctypes.byref(b)) == 0
         assert (a.value, b.value) == want
+    # Unit (half page) of the kernel layout: 32 x (radii row + 128 value codes + code row + 8
+    # scale bytes), i.e. the reference's bytes per token x 32 without the radius scale.
+    units = {(4, 4, 64, 0): 9472, (4, 8, 0, 1): 8448, (8, 2, 32, 0): 9344, (4, 2, 2, 0): 32 * (128 + 128 + 17 + 8)}
+    for (l1, deep, split, i8), want in units.items():
+        u = ctypes.c_int32()
+        assert lib.tp_unit_bytes(ctypes.byref(_lib.Format(l1, deep, split, i8)), ctypes.byref(u)) == 0
+        assert u.value == want and u.value % 16 == 0
     f = _lib.Format(3, 4, 64, 0)
     assert lib.tp_row_bytes(ctypes.byref(f), None, None) == _lib.TP_ERR_UNSUPPORTED
     assert "k_angle_bits_level1" in lib.tp_last_error().decode()
@@ -53,7 +60,7 @@ def test_version_and_row_bytes(lib):
 def test_error_statuses_map_to_reference_exceptions(lib):
     from turbopolar_b200 import _lib
     f = _lib.Format(4, 4, 64, 0)
-    pool = _lib.PagePool(None, None, None, None, None, None, 4, 0, f)
+    pool = _lib.PagePool(None, None, 4, 0, f)
     tail = _lib.Tail(None, None, 0)
     # Empty cache -> ValueError, before any launch.
     st = lib.tp_decode_attention(ctypes.byref(pool), ctypes.byref(tail), _lib.State(0, 0, 0, 0), None,
@@ -65,7 +72,7 @@ def test_error_statuses_map_to_reference_exceptions(lib):
     with pytest.raises(ValueError, match="divisible"):
         _lib.check(st)
     f2 = _lib.Format(4, 3, 64, 0)
-    pool2 = _lib.PagePool(None, None, None, None, None, None, 4, 0, f2)
+    pool2 = _lib.PagePool(None, None, 4, 0, f2)
     with pytest.raises(NotImplementedError):
         _lib.check(lib.tp_decode_pages(ctypes.byref(pool2), 0, 0, None, None, None))
 

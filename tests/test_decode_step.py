@@ -135,7 +135,7 @@ def test_decode_step_c_abi_errors():
     from turbopolar_b200 import _lib
     lib = _lib.lib()
     f = _lib.Format(4, 4, 64, 0)
-    pool = _lib.PagePool(None, None, None, None, None, None, 2, 0, f)
+    pool = _lib.PagePool(None, None, 2, 0, f)
     tail = _lib.Tail(16, 16, _lib.TP_F16)
     st = lib.tp_decode_step(ctypes.byref(pool), ctypes.byref(tail), None, 16, 16, _lib.TP_F16, 128, 16, 0, 4, 0.1,
                             16, None, 16, 1 << 20, None)

@@ -57,7 +57,7 @@ def test_noalloc_matches_workspace_entry_point_twice(lib):
 def test_noalloc_rejects_layouts_beyond_its_scratch(lib):
     from turbopolar_b200 import _lib
     f = _lib.Format(4, 4, 64, 0)
-    pool = _lib.PagePool(None, None, None, None, None, None, 4096, 0, f)
+    pool = _lib.PagePool(None, None, 4096, 0, f)
     tail = _lib.Tail(None, None, 0)
     st = lib.tp_decode_attention_noalloc(ctypes.byref(pool), ctypes.byref(tail), _lib.State(0, 1, 1, 0), None,
                                          ctypes.c_void_p(16), 0, 4096, 0.1, ctypes.c_void_p(16), None, None)

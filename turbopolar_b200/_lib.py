@@ -19,7 +19,7 @@ PARTIAL_FLOATS = 130
 STATE_WORDS = 6
 
 EXPORTED = (
-    "tp_row_bytes", "tp_encode_pages", "tp_append", "tp_decode_attention_workspace_size",
+    "tp_row_bytes", "tp_unit_bytes", "tp_encode_pages", "tp_append", "tp_decode_attention_workspace_size",
     "tp_decode_attention", "tp_decode_step", "tp_decode_attention_noalloc", "tp_combine_partials", "tp_fused_scores", "tp_decode_pages",
     "tp_export_pages", "tp_import_pages", "tp_last_error", "tp_version",
     "tp_exchange_bytes", "tp_ipc_alloc", "tp_ipc_open", "tp_ipc_close", "tp_ipc_free",
@@ -34,11 +34,28 @@ class Format(ctypes.Structure):
 
 
 class PagePool(ctypes.Structure):
+    """tp_page_pool: page blocks in the kernels' layout."""
+    _fields_ = [("pages", ctypes.c_void_p), ("radii_scales", ctypes.c_void_p),
+                ("num_kv_heads", ctypes.c_int32), ("page_capacity", ctypes.c_int32),
+                ("fmt", Format)]
+
+
+class BlockStore(ctypes.Structure):
+    """tp_block_store: pages in the reference's block-storage layout."""
     _fields_ = [("radii", ctypes.c_void_p), ("radii_scales", ctypes.c_void_p),
                 ("angle_codes_l1", ctypes.c_void_p), ("angle_codes_deep", ctypes.c_void_p),
                 ("v_codes", ctypes.c_void_p), ("v_scales", ctypes.c_void_p),
                 ("num_kv_heads", ctypes.c_int32), ("page_capacity", ctypes.c_int32),
                 ("fmt", Format)]
+
+
+def fmt_struct(fmt: dict) -> Format:
+    return Format(fmt["l1_bits"], fmt["deep_bits"], fmt["split_dim"], fmt["int8_radii"])
+
+
+def empty_pool(heads: int, fmt: dict) -> PagePool:
+    """A pool of capacity 0 (attention over the dense tail only)."""
+    return PagePool(None, None, heads, 0, fmt_struct(fmt))
 
 
 class Tail(ctypes.Structure):
@@ -62,6 +79,7 @@ def _declare(lib):
     P, I32, I64, SZ, F = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t, ctypes.c_float
     sig = {
         "tp_row_bytes": (ctypes.c_int, [ctypes.POINTER(Format), ctypes.POINTER(I32), ctypes.POINTER(I32)]),
+        "tp_unit_bytes": (ctypes.c_int, [ctypes.POINTER(Format), ctypes.POINTER(I32)]),
         "tp_encode_pages": (ctypes.c_int, [ctypes.POINTER(PagePool), P, P, I32, I64, I64, I64, I32, I32, P, P]),
         "tp_append": (ctypes.c_int, [ctypes.POINTER(PagePool), ctypes.POINTER(Tail), P, P, P, I32, I64, I64, I32, P]),
         "tp_decode_attention_workspace_size": (SZ, [I32, I32]),
@@ -74,8 +92,8 @@ def _declare(lib):
         "tp_combine_partials": (ctypes.c_int, [P, I32, I32, P, P]),
         "tp_fused_scores": (ctypes.c_int, [ctypes.POINTER(PagePool), I32, P, I32, I32, F, P, P]),
         "tp_decode_pages": (ctypes.c_int, [ctypes.POINTER(PagePool), I32, I32, P, P, P]),
-        "tp_export_pages": (ctypes.c_int, [ctypes.POINTER(PagePool), I32, I32, ctypes.POINTER(PagePool), P]),
-        "tp_import_pages": (ctypes.c_int, [ctypes.POINTER(PagePool), I32, I32, ctypes.POINTER(PagePool), P]),
+        "tp_export_pages": (ctypes.c_int, [ctypes.POINTER(PagePool), I32, I32, ctypes.POINTER(BlockStore), P]),
+        "tp_import_pages": (ctypes.c_int, [ctypes.POINTER(PagePool), I32, I32, ctypes.POINTER(BlockStore), P]),
         "tp_exchange_bytes": (SZ, [I32, I32]),
         "tp_ipc_alloc": (ctypes.c_int, [SZ, ctypes.POINTER(ctypes.c_void_p), P]),
         "tp_ipc_open": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_void_p)]),

@@ -89,8 +89,7 @@ class CudaKernelBridge:
         tail = _lib.Tail(tk.data_ptr(), tv.data_ptr(), _lib.TP_F16 if tdt == torch.float16 else _lib.TP_F32)
         if pool is None:
             fmt = config.format_fields()
-            st = _lib.PagePool(None, None, None, None, None, None, heads, 0,
-                               _lib.Format(fmt["l1_bits"], fmt["deep_bits"], fmt["split_dim"], fmt["int8_radii"]))
+            st = _lib.empty_pool(heads, fmt)
         else:
             st = pool.struct()
         out = torch.empty((B, Hq, 128), dtype=torch.float16, device=q.device)

@@ -191,9 +191,7 @@ class TurboPolarKVCacheRuntime:
             fills = self.tail_len + n == PAGE
             if fills:
                 self._ensure_capacity(self.n_pages + 1)
-            pool_struct = self.pool.struct() if self.pool is not None else _lib.PagePool(
-                None, None, None, None, None, None, self.heads, 0,
-                _lib.Format(self.fmt["l1_bits"], self.fmt["deep_bits"], self.fmt["split_dim"], self.fmt["int8_radii"]))
+            pool_struct = self.pool.struct() if self.pool is not None else _lib.empty_pool(self.heads, self.fmt)
             src_k = k[:, pos:pos + n]
             src_v = v[:, pos:pos + n]
             _lib.check(lib.tp_append(ctypes.byref(pool_struct), ctypes.byref(tail), self.d_state.data_ptr(),
@@ -243,8 +241,7 @@ class TurboPolarKVCacheRuntime:
     def pool_struct(self) -> _lib.PagePool:
         if self.pool is not None:
             return self.pool.struct()
-        f = _lib.Format(self.fmt["l1_bits"], self.fmt["deep_bits"], self.fmt["split_dim"], self.fmt["int8_radii"])
-        return _lib.PagePool(None, None, None, None, None, None, self.heads, 0, f)
+        return _lib.empty_pool(self.heads, self.fmt)
 
     def attention(self, q: torch.Tensor, scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
                   partial_out: Optional[torch.Tensor] = None, use_device_state: bool = False) -> torch.Tensor:

@@ -16,7 +16,7 @@ import ctypes
 import torch
 
 from . import _lib
-from .pages import PAGE, PagePool
+from .pages import PAGE, BlockStore, PagePool
 from .payload import PolarKeyBlock, QuantizedVBlock, block_metadata, format_of_metadata
 
 _VALUE_ONLY_FMT = dict(l1_bits=4, deep_bits=4, split_dim=64, int8_radii=0)
@@ -95,7 +95,7 @@ def pool_of_block(block: PolarKeyBlock, quant_v: QuantizedVBlock | None = None):
     else:
         vc = torch.zeros((B * H, S, PAGE, 128), dtype=torch.int8, device=radii.device)
         vs = torch.zeros((B * H, S, PAGE, 4), dtype=torch.float16, device=radii.device)
-    ref = PagePool.wrap_reference(
+    ref = BlockStore.wrap(
         radii.reshape(B * H, S, PAGE, 64).contiguous(),
         ex(block.angle_codes_l1).reshape(B * H, S, PAGE, -1).contiguous(),
         ex(block.angle_codes_deep).reshape(B * H, S, PAGE, -1).contiguous(), rs, vc, vs, fmt)
@@ -129,15 +129,15 @@ class GroupedVQuantizer:
         pool = PagePool(B * H, S, _VALUE_ONLY_FMT, v_block.device)
         flat = v_block.reshape(B * H, S * L, D)
         encode_pages(pool, flat, flat, S, 0)
-        ref = pool.export(0, S)
+        ref = pool.export(0, S, keys=False)
         return QuantizedVBlock(codes=ref.v_codes.view(B, H, S, L, D), scales=ref.v_scales.view(B, H, S, L, 4),
                                group_size=self.group_size)
 
     def dequantize_block(self, block: QuantizedVBlock) -> torch.Tensor:
         _require_cuda(block.codes)
         B, H, S, L, D = block.codes.shape
-        ref = PagePool.wrap_reference(None, None, None, None, block.codes.reshape(B * H, S, L, D).contiguous(),
-                                      block.scales.reshape(B * H, S, L, 4).contiguous(), _VALUE_ONLY_FMT)
+        ref = BlockStore.wrap(None, None, None, None, block.codes.reshape(B * H, S, L, D).contiguous(),
+                              block.scales.reshape(B * H, S, L, 4).contiguous(), _VALUE_ONLY_FMT)
         pool = PagePool.from_reference(ref)
         out = torch.empty((B * H, S * L, D), dtype=torch.float16, device=block.codes.device)
         _lib.check(_lib.lib().tp_decode_pages(ctypes.byref(pool.struct()), 0, S, None, out.data_ptr(),

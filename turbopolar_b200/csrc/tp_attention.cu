@@ -39,8 +39,21 @@
 
 namespace tp {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
+#ifndef TP_PRODUCER_WARPS
+#define TP_PRODUCER_WARPS 1
+#endif
+#ifndef TP_PRODUCER_LANES
+#define TP_PRODUCER_LANES 8
+#endif
+#ifndef TP_CONSUMERS
+#define TP_CONSUMERS 7
+#endif
+constexpr int kConsumers = TP_CONSUMERS;             // page-pass compute warps
+constexpr int kProducerWarps = TP_PRODUCER_WARPS;    // page-pass copy warps
+constexpr int kProducerLanes = TP_PRODUCER_LANES;    // issuing lanes per copy warp
+constexpr int kProducers = kProducerWarps * kProducerLanes;
+constexpr int kThreads = (kConsumers + kProducerWarps) * 32;
+constexpr int kMaxStages = 24;                   // ring stages (one unit each)
 constexpr int kMaxHeads = 8;  // query heads per unit (N of the mma)
 constexpr int kHalf = 32;     // tokens per unit
 // Records exchanged between CTAs and between GPUs: (m, l, o[128]) per query head, padded to
@@ -51,15 +64,11 @@ constexpr int kLutEntries = 256;
 constexpr int kMaxContrib = 192;  // CTAs that can share one head (grid <= kMaxContrib)
 
 struct AttnParams {
-  const uint8_t* radii;
+  const uint8_t* pages;
   const __half* radii_scales;
-  const uint8_t* l1;
-  const uint8_t* deep;
-  const int8_t* v_codes;
-  const __half* v_scales;
   int page_capacity;
-  int l1_bits, deep_bits, l1_pairs, l1_row, deep_row, radii_row, int8_radii;
-  int radii_page, l1_page, deep_page;  // bytes per page per head
+  int l1_bits, deep_bits, l1_pairs, l1_row, deep_row, code_row, radii_row, int8_radii;
+  int unit_bytes;  // bytes per half page (one bulk copy)
   void* tail_k;
   void* tail_v;
   int tail_f32;
@@ -85,8 +94,9 @@ struct AttnParams {
   float* partial_out;
   float* ws_partials;
   int* ws_error;
-  int stage_bytes, off_vcodes, off_l1, off_deep, off_vscales;
+  int stage_bytes, off_vcodes, off_codes, off_vscales;  // a stage holds one unit as laid out in the pool
   int smem_bar_off, smem_lut_off, smem_merge_off, smem_stage_off;
+  int n_stages;  // ring stages of the page pass
   uint32_t lut[2 * kLutEntries];  // half2 (cos, sin) per code: level-1 [0, 256), deep [256, 512)
 };
 
@@ -207,8 +217,8 @@ __device__ __forceinline__ void decode_row_fast(const uint8_t* stage, const Attn
                                                 int r, int t, uint32_t (&kp)[16]) {
   const uint4 R0 = lds128(stage + swz128(r, 2 * t));
   const uint4 R1 = lds128(stage + swz128(r, 2 * t + 1));
-  const uint8_t* cp = (t < 2) ? stage + P.off_l1 + r * 16 + 8 * t : stage + P.off_deep + r * 16 + 8 * (t - 2);
-  const uint2 C = lds64(cp);
+  // Row r's codes: 16 level-1 bytes then 16 deep bytes; lane t takes bytes [8t, 8t + 8).
+  const uint2 C = lds64(stage + P.off_codes + r * 32 + 8 * t);
   const uint32_t rw[8] = {R0.x, R0.y, R0.z, R0.w, R1.x, R1.y, R1.z, R1.w};
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
@@ -223,8 +233,8 @@ __device__ __forceinline__ void decode_row_fast(const uint8_t* stage, const Attn
 // General path: any supported format.  LUTs: level-1 at lut[0..255], deep at lut[256..511].
 __device__ __forceinline__ void decode_row_general(const uint8_t* stage, const AttnParams& P, const uint32_t* lut,
                                                    float radius_scale, int r, int t, uint32_t (&kp)[16]) {
-  const uint8_t* l1row = stage + P.off_l1 + r * P.l1_row;
-  const uint8_t* deeprow = stage + P.off_deep + r * P.deep_row;
+  const uint8_t* l1row = stage + P.off_codes + r * P.code_row;
+  const uint8_t* deeprow = l1row + P.l1_row;
 #pragma unroll 4
   for (int i = 0; i < 16; ++i) {
     const int j = 16 * t + i;
@@ -310,24 +320,14 @@ __device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, c
 }
 
 // ----------------------------------------------------------------------------- staging
-// Rows [32*half, 32*half + 32) of page `page` of KV head kvh into a half-page stage: one lane
-// issues one bulk copy per field (every field of a half page is contiguous in the pool
-// layout) completing on the stage's mbarrier.
+// Unit `half` of page `page` of KV head kvh into a stage: one bulk copy (every unit is
+// contiguous in the pool) completing on the stage's mbarrier.
 __device__ __forceinline__ void issue_half(uint8_t* stage, uint64_t* bar, const AttnParams& P, int kvh, int page,
                                            int half, uint64_t pol) {
-  const int64_t slot = int64_t(kvh) * P.page_capacity + page;
-  const uint32_t rb = kHalf * P.radii_row, lb = kHalf * P.l1_row, db = kHalf * P.deep_row;
+  const int64_t unit = (int64_t(kvh) * P.page_capacity + page) * 2 + half;
   fence_proxy_async_smem();
-  mbar_arrive_expect_tx(bar, rb + uint32_t(kHalf * kD) + lb + db + uint32_t(kHalf * 8));
-  bulk_g2s_hint(stage, P.radii + slot * P.radii_page + half * rb, rb, bar, pol);
-  bulk_g2s_hint(stage + P.off_vcodes,
-                reinterpret_cast<const uint8_t*>(P.v_codes) + slot * kVCodesPage + half * (kHalf * kD), kHalf * kD, bar,
-                pol);
-  if (lb) bulk_g2s_hint(stage + P.off_l1, P.l1 + slot * P.l1_page + half * lb, lb, bar, pol);
-  if (db) bulk_g2s_hint(stage + P.off_deep, P.deep + slot * P.deep_page + half * db, db, bar, pol);
-  bulk_g2s_hint(stage + P.off_vscales,
-                reinterpret_cast<const uint8_t*>(P.v_scales) + slot * kVScalesPage + half * (kHalf * 8), kHalf * 8, bar,
-                pol);
+  mbar_arrive_expect_tx(bar, uint32_t(P.unit_bytes));
+  bulk_g2s_hint(stage, P.pages + unit * P.unit_bytes, uint32_t(P.unit_bytes), bar, pol);
 }
 
 // Bounded wait for phase `parity` of a stage barrier (about a second); false on timeout.
@@ -422,15 +422,16 @@ __device__ __forceinline__ tp_state read_state(const AttnParams& P) {
   return st;
 }
 
-// This CTA's share of the page pass: units (half pages, head-major) [u0, u1), at most two
-// heads ("segments"), and warp `warp`'s contiguous slice of each segment.
+// This CTA's share of the page pass: units (half pages, head-major) [u0, u1) spanning at most
+// two heads ("segments"): n units, the first n0 of segment 0 (head vh_first) starting at its
+// unit a0, the rest of segment 1 starting at its unit 0.
 struct Part {
   int n_pages;
   bool active;
-  int vh_first, nseg, wa0, wn0, wa1, wn1, total;
+  int vh_first, nseg, n, n0, a0;
 };
 
-__device__ __forceinline__ Part make_part(const AttnParams& P, const tp_state& st, int c, int warp) {
+__device__ __forceinline__ Part make_part(const AttnParams& P, const tp_state& st, int c) {
   Part pt = {};
   pt.n_pages = min(max(st.n_pages, 0), P.page_capacity);
   const Grid g = grid_of(P.num_kv_heads * P.nqc, pt.n_pages, int(gridDim.x));
@@ -441,29 +442,54 @@ __device__ __forceinline__ Part make_part(const AttnParams& P, const tp_state& s
   pt.vh_first = u0 / uph;
   pt.nseg = (u1 - 1) / uph - pt.vh_first + 1;
   const int hb0 = pt.vh_first * uph;
-  const int a0 = u0 - hb0, n0 = min(u1, hb0 + uph) - u0;
-  pt.wa0 = a0 + (warp * n0) / kWarps;
-  pt.wn0 = a0 + ((warp + 1) * n0) / kWarps - pt.wa0;
-  if (pt.nseg > 1) {
-    const int n1 = u1 - (hb0 + uph);
-    pt.wa1 = (warp * n1) / kWarps;
-    pt.wn1 = ((warp + 1) * n1) / kWarps - pt.wa1;
-  }
-  pt.total = pt.wn0 + pt.wn1;
+  pt.n = u1 - u0;
+  pt.n0 = min(u1, hb0 + uph) - u0;
+  pt.a0 = u0 - hb0;
   return pt;
 }
 
+// Segment, page and half of CTA unit k.
+__device__ __forceinline__ int3 unit_ref(const Part& pt, int k) {
+  const int seg = k >= pt.n0 ? 1 : 0;
+  const int j = seg ? k - pt.n0 : pt.a0 + k;
+  return make_int3(seg, j >> 1, j & 1);
+}
+
+// Bounded wait for the producer (false on timeout).
+__device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity) { return stage_wait(bar, parity); }
+
+// Page pass.  Warps 0..kConsumers-1 compute; the kProducerWarps warps after them copy.
+// Consumer w takes CTA units w, w + kConsumers, ... and owns ring stages [w*S, w*S + S)
+// (S = P.n_stages / kConsumers), its j-th unit in stage w*S + j % S; each stage has a "full"
+// mbarrier (the bulk copy of a unit completes on it) and an "empty" one (the consumer releases
+// the stage).  Issuing lane p (lane i of producer warp v, p = v*kProducerLanes + i) serves the
+// consumers w = p (mod kProducers), their j-th units in turn, waiting for a stage's release
+// before reusing it.  Every stage has one producer and one consumer, so a wait is never more
+// than one phase ahead of its barrier.  A thread dispatches one bulk copy at a time, so the
+// copies are spread over several issuing lanes and never hold up the warps that compute;
+// consumers get the same number of units to within one.
 template <bool kFast>
 __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __grid_constant__ AttnParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ tp_state s_pre;  // cache state as read before the wait, one read for the CTA
   uint32_t* lut = reinterpret_cast<uint32_t*>(smem + P.smem_lut_off);
   float* merge = reinterpret_cast<float*>(smem + P.smem_merge_off);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.smem_bar_off);
+  uint64_t* empty = full + kMaxStages;
+  uint8_t* ring = smem + P.smem_stage_off;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int R = P.n_stages, S = R / kConsumers;
   const int gmax = P.gmax;
   const int rec_stride = gmax * TP_PARTIAL_FLOATS;
+  const bool producer = warp >= kConsumers;
+  const int pw = (warp - kConsumers) * kProducerLanes + lane;  // issuing-lane index
+  const bool issuer = producer && lane < kProducerLanes;
+  const int c = blockIdx.x;
+  const uint64_t pol = l2_evict_first_policy();
 
   // Before the previous kernel in the stream has completed (this grid is its programmatic
-  // dependent): only the code tables and the stage barriers, which depend on nothing it writes.
+  // dependent): the code tables, the ring barriers and the first copies, none of which
+  // depends on anything that kernel writes.
   {
     const int n1 = 1 << P.l1_bits, n2 = 1 << P.deep_bits;
     for (int i = tid; i < n1 + n2; i += kThreads) {
@@ -471,113 +497,134 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
       lut[j] = P.lut[j];
     }
   }
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.smem_bar_off) + warp * 2;
-  if (lane == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+  auto init_barriers = [&]() {
+    for (int st = 0; st < R; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], 1);
+    }
     fence_mbar_init();
+  };
+  if (tid == 0) {
+    init_barriers();
+    s_pre = read_state(P);
   }
-  __syncwarp();
-  const uint64_t pol = l2_evict_first_policy();
-  uint8_t* stages = smem + P.smem_stage_off + warp * 2 * P.stage_bytes;
-  const int c = blockIdx.x;
-
-  // The first two units of every warp go in flight before the wait, on the partition of the
-  // page count read now.  Every page below the newest one was written by a launch that had
-  // completed before the previous kernel in the stream started, so copies of those are valid
-  // whatever that kernel does; the newest page may be the one it is writing (an append that
-  // completed a page), so a warp whose first units touch it waits.  If the previous kernel
-  // changed the page count (it appended to this same cache), the copies are drained and the
-  // units reissued on the new partition.
-  Part pt = make_part(P, read_state(P), c, warp);
-  int seq0 = 0;      // stage-barrier sequence number of this warp's unit 0
-  int issued = 0;    // units of this warp in flight
-  auto issue = [&](int i) {
-    if (lane == 0 && i < pt.total) {
-      const bool s1 = i >= pt.wn0;
-      const int j = s1 ? pt.wa1 + (i - pt.wn0) : pt.wa0 + i;
-      const int q = seq0 + i;
-      issue_half(stages + (q & 1) * P.stage_bytes, &bars[q & 1], P, (pt.vh_first + (s1 ? 1 : 0)) / P.nqc, j >> 1,
-                 j & 1, pol);
+  __syncthreads();  // barriers initialised and the state read before any producer issues
+  Part pt = make_part(P, s_pre, c);
+  bool timed_out = false;
+  // Issue the j-th unit of consumer w (issuing lanes only).  After a release wait runs out
+  // nothing more is issued (the consumers' own bounded waits then run out and return).
+  auto produce = [&](int w, int j) {
+    const int slot = w * S + j % S, wrap = j / S;
+    if (wrap > 0 && !stage_wait(&empty[slot], uint32_t(wrap - 1) & 1u)) {
+      timed_out = true;
+      return;
+    }
+    const int3 u = unit_ref(pt, w + kConsumers * j);
+    issue_half(ring + slot * P.stage_bytes, &full[slot], P, (pt.vh_first + u.x) / P.nqc, u.y, u.z, pol);
+  };
+  // Units [j0, j1) of every consumer this lane serves, round by round.
+  auto produce_range = [&](int j0, int j1) {
+    for (int j = j0; j < j1; ++j) {
+      bool any = false;
+      for (int w = pw; w < kConsumers && !timed_out; w += kProducers) {
+        if (w + kConsumers * j >= pt.n) continue;
+        any = true;
+        produce(w, j);
+      }
+      if (!any || timed_out) break;
     }
   };
-  auto unit_page = [&](int i) {
-    const bool s1 = i >= pt.wn0;
-    return (s1 ? pt.wa1 + (i - pt.wn0) : pt.wa0 + i) >> 1;
-  };
-  {
-    const int early = min(2, pt.total);
-    bool safe = true;
-    for (int i = 0; i < early; ++i) safe = safe && unit_page(i) < pt.n_pages - 1;
-    if (safe) {
-      issue(0);
-      issue(1);
-      issued = early;
-    }
-  }
+  // Each consumer's first S units go in flight now, on the partition of the page count read
+  // now.  Every page below the newest one was written by a launch that had completed before
+  // the previous kernel in the stream started, so copies of those are valid whatever that
+  // kernel does; the newest page may be the one it is writing (an append that completed a
+  // page), so nothing is issued early if the first units touch it.
+  bool early = pt.active;
+  for (int k = 0; early && k < min(R, pt.n); ++k) early = unit_ref(pt, k).y < pt.n_pages - 1;
+  if (early && issuer) produce_range(0, S);
 
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
   // Let the split-combine grid become resident now; it waits for this grid to complete.
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
   const tp_state st = read_state(P);
-  bool timed_out = false;
   if (min(max(st.n_pages, 0), P.page_capacity) != pt.n_pages) {
-    for (int k = 0; k < issued; ++k)
-      if (!stage_wait(&bars[k], 0)) timed_out = true;
-    __syncwarp();
-    seq0 = issued;
-    issued = 0;
-    pt = make_part(P, st, c, warp);
+    // The previous kernel appended to this cache: let the early copies land, reset the
+    // barriers and start again on the new partition.
+    if (early && issuer) {
+      for (int j = 0; j < S; ++j)
+        for (int w = pw; w < kConsumers; w += kProducers)
+          if (w + kConsumers * j < pt.n && !stage_wait(&full[w * S + j], 0)) timed_out = true;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      for (int i = 0; i < R; ++i) {
+        mbar_inval(&full[i]);
+        mbar_inval(&empty[i]);
+      }
+      init_barriers();
+    }
+    early = false;
+    pt = make_part(P, st, c);
   }
-  if (issued == 0) {
-    issue(0);
-    issue(1);
-  }
+  __syncthreads();  // code tables; barriers reset if the partition changed
   if (!pt.active) {
-    if (timed_out && lane == 0) atomicExch(P.ws_error, 1);
+    if (timed_out) atomicExch(P.ws_error, 1);
     return;
   }
-  const int vh_first = pt.vh_first, nseg = pt.nseg;
-  const int wa0 = pt.wa0, wn0 = pt.wn0, wa1 = pt.wa1, wn1 = pt.wn1;
-  __syncthreads();  // code tables
-  WarpAcc A;
-  uint32_t qf[16];
-  for (int s = 0; s < nseg; ++s) {
-    const int vh = vh_first + s;
-    const int kvh = vh / P.nqc, chunk = vh % P.nqc;
-    const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
-    const int wn = s ? wn1 : wn0, wa = s ? wa1 : wa0;
-    const int i0 = s ? wn0 : 0;
-    if (wn > 0) {
-      load_q_frags(P, kvh * P.group + chunk * kMaxHeads, gc, lane, qf);
-      acc_reset(A);
+  const int n = pt.n, nseg = pt.nseg, vh_first = pt.vh_first;
+
+  if (producer) {
+    if (issuer) {
+      produce_range(early ? S : 0, (n + kConsumers - 1) / kConsumers);
+      if (timed_out) atomicExch(P.ws_error, 1);  // word 0: 1 after a wait ran out
     }
-    for (int i = i0; i < i0 + wn; ++i) {
-      const int q = seq0 + i;
-      const bool ready = stage_wait(&bars[q & 1], (q >> 1) & 1);
-      if (!ready) timed_out = true;
-      const int j = wa + (i - i0);
-      if (!ready) {
-        // Leave the unit out; the error word tells the host the result is unusable.
-      } else {
-        const int page = j >> 1, half = j & 1;
-        const int64_t pos0 = (int64_t(st.first_page) + page) * kPage + half * kHalf;
+  } else {
+    WarpAcc A;
+    uint32_t qf[16];
+    int cur = -1;        // segment of the accumulator (-1: none yet)
+    int kvh = 0, gc = gmax;
+    // Ring stage and phase of this warp's next unit.
+    int js = 0, wrap = 0;
+    for (int k = warp; k < n; k += kConsumers) {
+      const int3 u = unit_ref(pt, k);
+      if (u.x != cur) {
+        if (cur == 0) store_warp_partial(A, merge + warp * rec_stride, gc, lane);
+        else if (u.x == 1) store_empty_partial(merge + warp * rec_stride, gmax, lane);
+        cur = u.x;
+        const int vh = vh_first + cur, chunk = vh % P.nqc;
+        kvh = vh / P.nqc;
+        gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
+        load_q_frags(P, kvh * P.group + chunk * kMaxHeads, gc, lane, qf);
+        acc_reset(A);
+      }
+      const int slot = warp * S + js;
+      const bool ready = stage_wait(&full[slot], uint32_t(wrap) & 1u);
+      if (ready) {
+        const int64_t pos0 = (int64_t(st.first_page) + u.y) * kPage + u.z * kHalf;
         const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, kHalf));
         float rs = 0.f;
-        if (P.int8_radii) rs = __half2float(P.radii_scales[int64_t(kvh) * P.page_capacity + page]);
-        process_half<kFast>(A, stages + (q & 1) * P.stage_bytes, P, lut, qf, rs, vt, lane);
+        if (P.int8_radii) rs = __half2float(P.radii_scales[int64_t(kvh) * P.page_capacity + u.y]);
+        process_half<kFast>(A, ring + slot * P.stage_bytes, P, lut, qf, rs, vt, lane);
+      } else {
+        timed_out = true;  // the unit is left out; the error word marks the result unusable
       }
       __syncwarp();
-      issue(i + 2);
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (++js == S) { js = 0; ++wrap; }
     }
-    // Segment 0 partials live in the merge region; segment 1 partials in the warp's own
-    // stage buffers, free once its pipeline has drained.
-    float* rec = s == 0 ? merge + warp * rec_stride : reinterpret_cast<float*>(stages);
-    if (wn > 0) store_warp_partial(A, rec, gc, lane);
-    else store_empty_partial(rec, gc, lane);
+    // Segment 0 partials go to the merge region now; segment 1 partials to this warp's ring
+    // stage once every consumer is done with the ring (all issued copies have landed).
+    if (cur == 0) store_warp_partial(A, merge + warp * rec_stride, gc, lane);
+    else if (cur == -1) store_empty_partial(merge + warp * rec_stride, gmax, lane);
+    if (timed_out && lane == 0) atomicExch(P.ws_error, 1);  // word 0: 1 after a stage-wait timeout
+    asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers * 32) : "memory");
+    if (nseg > 1) {
+      float* rec1 = reinterpret_cast<float*>(ring + warp * P.stage_bytes);
+      if (cur == 1) store_warp_partial(A, rec1, gc, lane);
+      else store_empty_partial(rec1, gmax, lane);
+    }
   }
-  if (timed_out && lane == 0) atomicExch(P.ws_error, 1);  // word 0: 1 after a stage-wait timeout
   __syncthreads();
 
   // Merge the warps of each segment and publish this CTA's partial; the split-combine kernel
@@ -587,20 +634,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
     const int chunk = vh % P.nqc;
     const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
     float* slot = P.ws_partials + int64_t(c * 2 + s) * kPartialStride;
-    const float* recs = s == 0 ? merge : reinterpret_cast<const float*>(smem + P.smem_stage_off);
-    const int wstride = s == 0 ? rec_stride : 2 * P.stage_bytes / int(sizeof(float));
+    const float* recs = s == 0 ? merge : reinterpret_cast<const float*>(ring);
+    const int wstride = s == 0 ? rec_stride : P.stage_bytes / int(sizeof(float));
 #pragma unroll 1
     for (int i = tid; i < gc * kD; i += kThreads) {
       const int h = i >> 7, d = i & (kD - 1);
-      float m[kWarps];
+      float m[kConsumers];
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) m[w] = recs[w * wstride + h * TP_PARTIAL_FLOATS];
+      for (int w = 0; w < kConsumers; ++w) m[w] = recs[w * wstride + h * TP_PARTIAL_FLOATS];
       float M = m[0];
 #pragma unroll
-      for (int w = 1; w < kWarps; ++w) M = fmaxf(M, m[w]);
+      for (int w = 1; w < kConsumers; ++w) M = fmaxf(M, m[w]);
       float L = 0.f, O = 0.f;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
+      for (int w = 0; w < kConsumers; ++w) {
         const float* r = recs + w * wstride + h * TP_PARTIAL_FLOATS;
         const float f = (m[w] == -INFINITY) ? 0.f : exp2_approx(m[w] - M);
         L = fmaf(r[1], f, L);
@@ -722,14 +769,12 @@ __device__ __forceinline__ void block_partial(const AttnParams& P, int qh, int v
   __syncthreads();
 }
 
-// One page of one KV head held in shared memory in the pool layout (the fused step's flush).
+// One page of one KV head held in shared memory, laid out as a pool page block (the fused
+// step's flush).
 struct SmemPage {
-  uint8_t codes[kPage * kPairs];     // encode scratch: one code per pair
-  float red[8];                      // encode scratch: block reduction
-  __align__(16) uint8_t radii[kPage * kPairs * 2];
-  __align__(16) uint8_t angles[kPage * kPairs];  // level-1 rows, then deep rows
-  __align__(16) uint8_t v_codes[kVCodesPage];
-  __align__(16) __half v_scales[kPage * 4];
+  uint8_t codes[kPage * kPairs];  // encode scratch: one code per pair
+  float red[8];                   // encode scratch: block reduction
+  __align__(16) uint8_t block[kMaxPageBytes];
   __half radii_scale;
 };
 
@@ -741,61 +786,47 @@ union CombineSmem {
 // Key and value channels 4*lane .. 4*lane+3 of token t of the shared-memory page, decoded as
 // rfsn_v11/quant/polar/decoder.py:36-67 and v_quant/encoder.py:32-38 do (cos and sin of the
 // code angle from the float16 table the page pass uses).
-__device__ __forceinline__ float4 page_token(const AttnParams& P, const SmemPage& pg, int t, int lane, bool key) {
+__device__ __forceinline__ float4 page_token(const AttnParams& P, SmemPage& pg, int t, int lane, bool key) {
+  const PoolArgs& W = P.wpool;
   if (!key) {
     float vx[4];
+    const float s = __half2float(*vscale_at(W, pg.block, t, lane >> 3));
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int d = 4 * lane + e;
-      const int8_t code = int8_t(pg.v_codes[vcode_offset(t, d)] ^ 0x80u);
-      vx[e] = __half2float(__float2half_rn(float(code) * __half2float(pg.v_scales[vscale_index(t, d >> 5)])));
+      const int8_t code = int8_t(*vcode_at(W, pg.block, t, 4 * lane + e) ^ 0x80u);
+      vx[e] = __half2float(__float2half_rn(float(code) * s));
     }
     return make_float4(vx[0], vx[1], vx[2], vx[3]);
   }
   float kx[4];
   const uint32_t* lut = P.lut;
+  const uint8_t* row = codes_at(W, pg.block, t);
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
     const int j = 2 * lane + e;
     uint32_t code, cs;
     if (j < P.l1_pairs) {
-      const uint8_t* row = pg.angles + t * P.l1_row;
       code = P.l1_bits == 8 ? row[j] : (row[j >> 1] >> (4 * (j & 1))) & 15u;
       cs = lut[code];
     } else {
-      const uint8_t* row = pg.angles + kPage * P.l1_row + t * P.deep_row;
+      const uint8_t* drow = row + P.l1_row;
       const int rel = j - P.l1_pairs;
-      if (P.deep_bits == 8) code = row[rel];
-      else if (P.deep_bits == 4) code = (row[rel >> 1] >> (4 * (rel & 1))) & 15u;
-      else code = (row[rel >> 2] >> (2 * (rel & 3))) & 3u;
+      if (P.deep_bits == 8) code = drow[rel];
+      else if (P.deep_bits == 4) code = (drow[rel >> 1] >> (4 * (rel & 1))) & 15u;
+      else code = (drow[rel >> 2] >> (2 * (rel & 3))) & 3u;
       cs = lut[kLutEntries + code];
     }
     float r;
     if (P.int8_radii) {
-      r = expf(float(reinterpret_cast<const int8_t*>(pg.radii)[t * kPairs + j]) * __half2float(pg.radii_scale));
+      r = expf(float(*radius_i8_at(W, pg.block, t, j)) * __half2float(pg.radii_scale));
     } else {
-      r = __half2float(*reinterpret_cast<const __half*>(pg.radii + radii_f16_offset(t, j)));
+      r = __half2float(*radius_f16_at(W, pg.block, t, j));
     }
     const float2 c2 = __half22float2(u32_as_h2(cs));
     kx[2 * e] = __half2float(__float2half_rn(r * c2.x));
     kx[2 * e + 1] = __half2float(__float2half_rn(r * c2.y));
   }
   return make_float4(kx[0], kx[1], kx[2], kx[3]);
-}
-
-// Copy the encoded shared-memory page to pool page `page` of KV head kvh.
-__device__ __forceinline__ void store_page(const AttnParams& P, const SmemPage& pg, int kvh, int page) {
-  const PagePtrs dst = P.wpool.page(kvh, page);
-  const int rb = kPage * P.radii_row, lb = kPage * P.l1_row, db = kPage * P.deep_row;
-  for (int i = threadIdx.x; i < rb / 16; i += blockDim.x)
-    reinterpret_cast<uint4*>(dst.radii)[i] = reinterpret_cast<const uint4*>(pg.radii)[i];
-  for (int i = threadIdx.x; i < lb; i += blockDim.x) dst.l1[i] = pg.angles[i];
-  for (int i = threadIdx.x; i < db; i += blockDim.x) dst.deep[i] = pg.angles[lb + i];
-  for (int i = threadIdx.x; i < int(kVCodesPage / 16); i += blockDim.x)
-    reinterpret_cast<uint4*>(dst.v_codes)[i] = reinterpret_cast<const uint4*>(pg.v_codes)[i];
-  for (int i = threadIdx.x; i < int(kVScalesPage / 16); i += blockDim.x)
-    reinterpret_cast<uint4*>(dst.v_scales)[i] = reinterpret_cast<const uint4*>(pg.v_scales)[i];
-  if (threadIdx.x == 0 && P.int8_radii) *dst.radii_scale = pg.radii_scale;
 }
 
 template <typename T>
@@ -816,20 +847,12 @@ template <typename T>
 __device__ __noinline__ float3 flush_partial(const AttnParams& P, CombineSmem& sm, int kvh, int qh, int page,
                                               bool store, int valid, float* s_sc, float* s_o) {
   SmemPage& pg = sm.page;
-  PagePtrs dst;
-  dst.radii = pg.radii;
-  dst.radii_scale = &pg.radii_scale;
-  dst.l1 = pg.angles;
-  dst.deep = pg.angles + kPage * P.l1_row;
-  dst.v_codes = reinterpret_cast<int8_t*>(pg.v_codes);
-  dst.v_scales = pg.v_scales;
   const T* tk = static_cast<const T*>(P.tail_k) + int64_t(kvh) * kPage * kD;
   const T* tv = static_cast<const T*>(P.tail_v) + int64_t(kvh) * kPage * kD;
-  encode_page<T>(tk, tv, kD, dst, P.wpool, pg.codes, pg.red, pg.v_codes, pg.v_scales,
+  encode_page<T>(tk, tv, kD, P.wpool, pg.block, &pg.radii_scale, pg.codes, pg.red,
                  static_cast<const T*>(P.k_new) + int64_t(kvh) * P.new_head_stride,
                  static_cast<const T*>(P.v_new) + int64_t(kvh) * P.new_head_stride);
-  __syncthreads();
-  if (store) store_page(P, pg, kvh, page);
+  if (store) store_page_block(P.wpool, pg.block, pg.radii_scale, kvh, page);
   float M = -INFINITY, L = 0.f, O = 0.f;
   block_partial(P, qh, valid, [&](int t, int lane, bool key) { return page_token(P, pg, t, lane, key); }, s_sc, s_o,
                 M, L, O);
@@ -1130,6 +1153,29 @@ static int num_sms() {
   return g_num_sms;
 }
 
+// Dynamic shared memory the page pass may use: the opt-in per-block limit, and no more than
+// leaves room on one SM for a split-combine CTA beside it.
+static int ring_budget(const void* page_pass) {
+  static int budget = 0;
+  if (budget == 0) {
+    int dev = 0, per_sm = 233472, per_block = 232448, reserved = 1024;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&per_block, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    cudaFuncAttributes comb = {}, pp = {};
+    cudaFuncGetAttributes(&comb, reinterpret_cast<const void*>(split_combine_kernel));
+    cudaFuncGetAttributes(&pp, page_pass);
+#ifdef EXP_FULL_RING
+    budget = per_block - int(pp.sharedSizeBytes) - 256;
+#else
+    budget = min(per_block - int(pp.sharedSizeBytes),
+                 per_sm - 2 * reserved - int(comb.sharedSizeBytes) - int(pp.sharedSizeBytes)) - 256;
+#endif
+  }
+  return budget;
+}
+
 static int grid_size(int num_kv_heads, int num_q_heads) {
   const int group = num_q_heads / num_kv_heads;
   const int nqc = (group + kMaxHeads - 1) / kMaxHeads;
@@ -1184,23 +1230,18 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
   if ((reinterpret_cast<uintptr_t>(q) & 15)) return fail(TP_ERR_INVALID, "q must be 16-byte aligned");
 
   AttnParams P;
-  P.radii = static_cast<const uint8_t*>(pool->radii);
+  P.pages = static_cast<const uint8_t*>(pool->pages);
   P.radii_scales = static_cast<const __half*>(pool->radii_scales);
-  P.l1 = static_cast<const uint8_t*>(pool->angle_codes_l1);
-  P.deep = static_cast<const uint8_t*>(pool->angle_codes_deep);
-  P.v_codes = static_cast<const int8_t*>(pool->v_codes);
-  P.v_scales = static_cast<const __half*>(pool->v_scales);
   P.page_capacity = pool->page_capacity;
   P.l1_bits = pool->fmt.l1_bits;
   P.deep_bits = pool->fmt.deep_bits;
   P.l1_pairs = L.l1_pairs;
   P.l1_row = L.l1_row;
   P.deep_row = L.deep_row;
+  P.code_row = L.code_row;
   P.radii_row = L.radii_row;
   P.int8_radii = pool->fmt.int8_radii;
-  P.radii_page = int(L.radii_page);
-  P.l1_page = int(L.l1_page);
-  P.deep_page = int(L.deep_page);
+  P.unit_bytes = L.unit_bytes;
   P.tail_k = tail->k;
   P.tail_v = tail->v;
   P.tail_f32 = tail->dtype == TP_F32;
@@ -1244,25 +1285,29 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
     P.xrank = x->rank;
   }
   P.ws_partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
-  // Half-page stage: radii | v codes | level-1 codes | 64-byte bank shift | deep codes | v scales.
+  // Half-page stage: one unit copied linearly (radii | v codes | angle codes | v scales).
   auto up = [](int x, int a) { return (x + a - 1) / a * a; };
-  P.off_vcodes = kHalf * P.radii_row;
-  P.off_l1 = P.off_vcodes + kHalf * kD;
-  P.off_deep = P.off_l1 + up(kHalf * P.l1_row, 128) + 64;
-  P.off_vscales = up(P.off_deep + kHalf * P.deep_row, 128);
-  P.stage_bytes = up(P.off_vscales + kHalf * 8, 128);
-  const int merge_bytes = kWarps * P.gmax * TP_PARTIAL_FLOATS * int(sizeof(float));
-  P.smem_bar_off = 0;                       // 2 stage barriers per warp
-  P.smem_lut_off = 128;
+  P.off_vcodes = L.u_vcodes;
+  P.off_codes = L.u_codes;
+  P.off_vscales = L.u_vscales;
+  P.stage_bytes = up(L.unit_bytes, 128);
+  const int merge_bytes = kConsumers * P.gmax * TP_PARTIAL_FLOATS * int(sizeof(float));
+  P.smem_bar_off = 0;                       // full and empty barrier per ring stage
+  P.smem_lut_off = up(2 * kMaxStages * 8, 128);
   P.smem_merge_off = P.smem_lut_off + 2 * kLutEntries * 4;
   P.smem_stage_off = up(P.smem_merge_off + merge_bytes, 128);
-  const int stage_region = kWarps * 2 * P.stage_bytes;
-  const int smem = P.smem_stage_off + stage_region;
 
   const bool fast = P.l1_bits == 4 && P.deep_bits == 4 && pool->fmt.split_dim == 64 && !P.int8_radii;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const void* fn = fast ? reinterpret_cast<const void*>(decode_attention_kernel<true>)
                         : reinterpret_cast<const void*>(decode_attention_kernel<false>);
+  // Ring stages: as many as fit while a split-combine CTA still fits beside the page-pass CTA
+  // on one SM (so it starts, and finishes the dense tail, while the page pass runs).
+  const int ring_bytes = ring_budget(fn) - P.smem_stage_off;
+  P.n_stages = min(kMaxStages, ring_bytes / P.stage_bytes) / kConsumers * kConsumers;
+  if (P.n_stages < 2 * kConsumers)
+    return fail(TP_ERR_UNSUPPORTED, "tp_decode_attention: not enough shared memory for the page ring");
+  const int smem = P.smem_stage_off + P.n_stages * P.stage_bytes;
   static int attr_bytes[2] = {0, 0};
   int& have = attr_bytes[fast ? 1 : 0];
   if (smem > have) {

@@ -14,60 +14,9 @@
 
 namespace tp {
 
-// Pointers of one (head, page) of the pool.
-struct PagePtrs {
-  uint8_t* radii;
-  __half* radii_scale;
-  uint8_t* l1;
-  uint8_t* deep;
-  int8_t* v_codes;
-  __half* v_scales;
-};
-
-struct PoolArgs {
-  uint8_t* radii;
-  __half* radii_scales;
-  uint8_t* l1;
-  uint8_t* deep;
-  int8_t* v_codes;
-  __half* v_scales;
-  int num_kv_heads, page_capacity;
-  int l1_bits, deep_bits, split_dim, int8_radii;
-  int l1_pairs, l1_row, deep_row, radii_row;
-
-  __device__ PagePtrs page(int h, int p) const {
-    const int64_t slot = int64_t(h) * page_capacity + p;
-    PagePtrs d;
-    d.radii = radii + slot * kPage * radii_row;
-    d.radii_scale = int8_radii ? radii_scales + slot : nullptr;
-    d.l1 = l1 + slot * kPage * l1_row;
-    d.deep = deep + slot * kPage * deep_row;
-    d.v_codes = v_codes + slot * kVCodesPage;
-    d.v_scales = v_scales + slot * kPage * 4;
-    return d;
-  }
-};
-
-inline PoolArgs pool_args(const tp_page_pool& p, const Layout& L) {
-  PoolArgs a;
-  a.radii = static_cast<uint8_t*>(p.radii);
-  a.radii_scales = static_cast<__half*>(p.radii_scales);
-  a.l1 = static_cast<uint8_t*>(p.angle_codes_l1);
-  a.deep = static_cast<uint8_t*>(p.angle_codes_deep);
-  a.v_codes = static_cast<int8_t*>(p.v_codes);
-  a.v_scales = static_cast<__half*>(p.v_scales);
-  a.num_kv_heads = p.num_kv_heads;
-  a.page_capacity = p.page_capacity;
-  a.l1_bits = p.fmt.l1_bits;
-  a.deep_bits = p.fmt.deep_bits;
-  a.split_dim = p.fmt.split_dim;
-  a.int8_radii = p.fmt.int8_radii;
-  a.l1_pairs = L.l1_pairs;
-  a.l1_row = L.l1_row;
-  a.deep_row = L.deep_row;
-  a.radii_row = L.radii_row;
-  return a;
-}
+// Largest page block of any supported format: float16 radii, 64 code bytes per token.
+constexpr int kMaxUnitBytes = kUnit * 128 + kVCodesUnit + kUnit * 64 + kVScalesUnit;
+constexpr int kMaxPageBytes = 2 * kMaxUnitBytes;
 
 // ----------------------------------------------------------------------------- codec math
 struct PairCode {
@@ -137,12 +86,14 @@ template <typename T> __device__ __forceinline__ float to_f(T x);
 template <> __device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
 template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }
 
-// Encode one 64-token page of one head.  256 threads: thread (token l = tid/4, quarter c = tid%4)
-// owns pairs [16c, 16c+16) and V group c of token l.
+// Encode one 64-token page of one head into the page block s_page (shared memory, laid out
+// as in the pool) and its radius scale into *s_radius_scale (int8 radii only).  256 threads:
+// thread (token l = tid/4, quarter c = tid%4) owns pairs [16c, 16c+16) and V group c of
+// token l.  Ends with a barrier, so the caller may copy the block out.
 template <typename T>
-__device__ void encode_page(const T* k_rows, const T* v_rows, int64_t row_stride, const PagePtrs& dst,
-                            const PoolArgs& P, uint8_t* s_codes, float* s_red, uint8_t* s_v, __half* s_scales,
-                            const T* k_last = nullptr, const T* v_last = nullptr) {
+__device__ void encode_page(const T* k_rows, const T* v_rows, int64_t row_stride, const PoolArgs& P, uint8_t* s_page,
+                            __half* s_radius_scale, uint8_t* s_codes, float* s_red, const T* k_last = nullptr,
+                            const T* v_last = nullptr) {
   const int tid = threadIdx.x;
   const int l = tid >> 2, c = tid & 3;
   const bool f16_in = sizeof(T) == 2;
@@ -166,7 +117,7 @@ __device__ void encode_page(const T* k_rows, const T* v_rows, int64_t row_stride
 #pragma unroll
       for (int i = 0; i < 4; ++i)
         w[i] = uint32_t(__half_as_ushort(rad[8 * h + 2 * i])) | (uint32_t(__half_as_ushort(rad[8 * h + 2 * i + 1])) << 16);
-      *reinterpret_cast<uint4*>(dst.radii + radii_f16_offset(l, 16 * c + 8 * h)) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(radius_f16_at(P, s_page, l, 16 * c + 8 * h)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   } else {
     // encoder.py:38-45: one scale per (head, block) = max|log r| / 127.
@@ -182,13 +133,13 @@ __device__ void encode_page(const T* k_rows, const T* v_rows, int64_t row_stride
     const float ls = (m == 0.0f) ? 1e-6f : m;
     const __half sc = __float2half_rn(__fdiv_rn(ls, 127.0f));
     const float scf = __half2float(sc);
-    int8_t* rr = reinterpret_cast<int8_t*>(dst.radii) + l * kPairs + 16 * c;
+    int8_t* rr = radius_i8_at(P, s_page, l, 16 * c);
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const float q = rintf(__fdiv_rn(logr[i], scf));
       rr[i] = static_cast<int8_t>(fminf(fmaxf(q, -128.0f), 127.0f));
     }
-    if (tid == 0) *dst.radii_scale = sc;
+    if (tid == 0) *s_radius_scale = sc;
   }
   // Values: group c of token l.
   {
@@ -203,41 +154,40 @@ __device__ void encode_page(const T* k_rows, const T* v_rows, int64_t row_stride
     const __half sc = v_group_scale(mx, f16_in);
     const float scf = __half2float(sc);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) s_v[vcode_offset(l, 32 * c + i)] = uint8_t(v_code(vals[i], scf, f16_in)) ^ 0x80u;
-    s_scales[vscale_index(l, c)] = sc;
+    for (int i = 0; i < 32; ++i) *vcode_at(P, s_page, l, 32 * c + i) = uint8_t(v_code(vals[i], scf, f16_in)) ^ 0x80u;
+    *vscale_at(P, s_page, l, c) = sc;
   }
   __syncthreads();
-  // Pack the angle codes row by row (encoder.py:56-75, :100-130).
-  const int l1_bytes = kPage * P.l1_row, deep_bytes = kPage * P.deep_row;
-  for (int i = tid; i < l1_bytes + deep_bytes; i += blockDim.x) {
-    const bool is_l1 = i < l1_bytes;
-    const int ii = is_l1 ? i : i - l1_bytes;
-    const int row = is_l1 ? P.l1_row : P.deep_row;
-    const int tok = ii / row, byte = ii % row;
+  // Pack the angle codes row by row (encoder.py:56-75, :100-130): level-1 bytes, then deep.
+  for (int i = tid; i < kPage * P.code_row; i += blockDim.x) {
+    const int tok = i / P.code_row, byte = i - tok * P.code_row;
+    const bool is_l1 = byte < P.l1_row;
+    const int bb = is_l1 ? byte : byte - P.l1_row;
     const int bits = is_l1 ? P.l1_bits : P.deep_bits;
     const int n = is_l1 ? P.l1_pairs : kPairs - P.l1_pairs;
     const uint8_t* codes = s_codes + tok * kPairs + (is_l1 ? 0 : P.l1_pairs);
     uint8_t out;
     if (bits == 8) {
-      out = codes[byte];
+      out = codes[bb];
     } else {
       const int per = 8 / bits, mask = (1 << bits) - 1;
       out = 0;
       for (int q = 0; q < per; ++q) {
-        const int idx = byte * per + q;
+        const int idx = bb * per + q;
         if (idx < n) out |= uint8_t((codes[idx] & mask) << (q * bits));
       }
     }
-    (is_l1 ? dst.l1 : dst.deep)[ii] = out;
+    codes_at(P, s_page, tok)[byte] = out;
   }
-  // Values and scales, staged in the page layout, leave in 16-byte stores (unless the page
-  // itself lives in shared memory at the staging buffers).
-  if (reinterpret_cast<const void*>(dst.v_codes) != reinterpret_cast<const void*>(s_v)) {
-    for (int i = tid; i < int(kVCodesPage / 16); i += blockDim.x)
-      reinterpret_cast<uint4*>(dst.v_codes)[i] = reinterpret_cast<const uint4*>(s_v)[i];
-    for (int i = tid; i < int(kVScalesPage / 16); i += blockDim.x)
-      reinterpret_cast<uint4*>(dst.v_scales)[i] = reinterpret_cast<const uint4*>(s_scales)[i];
-  }
+  __syncthreads();
+}
+
+// Copy an encoded page block from shared memory to pool page `page` of head h (all threads).
+__device__ __forceinline__ void store_page_block(const PoolArgs& P, const uint8_t* s_page, __half radius_scale, int h,
+                                                 int page) {
+  uint4* dst = reinterpret_cast<uint4*>(P.page(h, page));
+  for (int i = threadIdx.x; i < P.page_bytes / 16; i += blockDim.x) dst[i] = reinterpret_cast<const uint4*>(s_page)[i];
+  if (threadIdx.x == 0 && P.int8_radii) *P.radii_scale(h, page) = radius_scale;
 }
 
 }  // namespace tp

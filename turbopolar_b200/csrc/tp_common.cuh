@@ -17,50 +17,126 @@ int fail(int status, const std::string& msg);
 int check_launch(const char* what);
 
 // ----------------------------------------------------------------------------- format
-struct Layout {
-  int l1_pairs, deep_pairs;      // pairs coded at level 1 / deep
-  int l1_row, deep_row;          // packed bytes per token row
-  int radii_row;                 // bytes per token row of radii (128 fp16, 64 int8)
-  int64_t radii_page, l1_page, deep_page;  // bytes per page per head
-};
-// Returns TP_OK or TP_ERR_UNSUPPORTED.
-int make_layout(const tp_format& f, Layout* out);
-// Checks a pool's format, sizes and pointers (key fields only when `keys`).
-int validate_pool(const tp_page_pool* pool, Layout* L, bool keys = true);
-
 constexpr int kPage = TP_PAGE_TOKENS;  // tokens per page
 constexpr int kD = TP_HEAD_DIM;        // head dim
 constexpr int kPairs = kD / 2;
+constexpr int kUnit = kPage / 2;       // tokens per unit (half page)
 constexpr int64_t kVCodesPage = kPage * kD;   // int8 bytes per page per head
 constexpr int64_t kVScalesPage = kPage * 4 * 2;  // fp16 [64][4]
+constexpr int kVCodesUnit = kUnit * kD;       // 4096
+constexpr int kVScalesUnit = kUnit * 4 * 2;   // 256
+
+struct Layout {
+  int l1_pairs, deep_pairs;      // pairs coded at level 1 / deep
+  int l1_row, deep_row;          // packed bytes per token row
+  int code_row;                  // l1_row + deep_row: one token's codes in a unit
+  int radii_row;                 // bytes per token row of radii (128 fp16, 64 int8)
+  int u_vcodes, u_codes, u_vscales, unit_bytes;  // byte offsets inside a unit, unit size
+  int page_bytes;                // 2 * unit_bytes
+};
+// Returns TP_OK or TP_ERR_UNSUPPORTED.
+int make_layout(const tp_format& f, Layout* out);
+// Checks a pool's format, sizes and pointers.
+int validate_pool(const tp_page_pool* pool, Layout* L);
+// Checks a reference-layout block store (key fields only when `keys`).
+int validate_store(const tp_block_store* ref, Layout* L, bool keys);
+
+// Device view of a page pool.
+struct PoolArgs {
+  uint8_t* pages;
+  __half* radii_scales;
+  int num_kv_heads, page_capacity;
+  int l1_bits, deep_bits, split_dim, int8_radii;
+  int l1_pairs, l1_row, deep_row, code_row, radii_row;
+  int u_vcodes, u_codes, u_vscales, unit_bytes, page_bytes;
+
+  __host__ __device__ uint8_t* page(int h, int p) const {
+    return pages + (int64_t(h) * page_capacity + p) * page_bytes;
+  }
+  __host__ __device__ __half* radii_scale(int h, int p) const {
+    return int8_radii ? radii_scales + int64_t(h) * page_capacity + p : nullptr;
+  }
+};
+
+inline PoolArgs pool_args(const tp_page_pool& p, const Layout& L) {
+  PoolArgs a;
+  a.pages = static_cast<uint8_t*>(p.pages);
+  a.radii_scales = static_cast<__half*>(p.radii_scales);
+  a.num_kv_heads = p.num_kv_heads;
+  a.page_capacity = p.page_capacity;
+  a.l1_bits = p.fmt.l1_bits;
+  a.deep_bits = p.fmt.deep_bits;
+  a.split_dim = p.fmt.split_dim;
+  a.int8_radii = p.fmt.int8_radii;
+  a.l1_pairs = L.l1_pairs;
+  a.l1_row = L.l1_row;
+  a.deep_row = L.deep_row;
+  a.code_row = L.code_row;
+  a.radii_row = L.radii_row;
+  a.u_vcodes = L.u_vcodes;
+  a.u_codes = L.u_codes;
+  a.u_vscales = L.u_vscales;
+  a.unit_bytes = L.unit_bytes;
+  a.page_bytes = L.page_bytes;
+  return a;
+}
 
 // ----------------------------------------------------------------------------- page layout in HBM
-// The codes are the reference's, bit for bit; their order inside a page is chosen for the
-// decode kernel (tp_export_pages / tp_import_pages convert to and from the reference layout):
+// The codes are the reference's, bit for bit; their placement is chosen for the decode kernel
+// (tp_export_pages / tp_import_pages convert to and from the reference layout).  A page block
+// is two units (tokens 0-31, 32-63) of PoolArgs::unit_bytes each; inside a unit, for token
+// row l = 0..31:
 //
-// * float16 radii, row l (token) of 128 bytes: 16-byte chunk c (pairs 8c..8c+7) is stored at
-//   chunk c ^ (l & 7), the XOR swizzle that makes the kernel's row-fragment loads
-//   bank-conflict free once a page is copied linearly into shared memory.  int8 radii rows are
-//   64 bytes and stay linear.
-// * value codes, stored as (code ^ 0x80) -- i.e. code + 128 as a byte -- in mma fragment order:
-//   token l = 16*kk + 8*a + 2*t + b (kk: 16-token step, a: upper/lower 8, t: lane quad column,
-//   b: pair bit) and channel d = 32*G + 4*g + 2*e_hi + e_lo sit at byte
-//   kk*2048 + G*512 + g*64 + t*16 + a*8 + e_hi*4 + e_lo*2 + b,
-//   so lane 4g+t of a warp finds its whole A fragment for group G of step kk in one 16-byte word.
-// * value scales (float16, one per token and 32-channel group) at half index
+// * radii at offset 0: float16 rows of 128 bytes, 16-byte chunk c (pairs 8c..8c+7) stored at
+//   chunk c ^ (l & 7), the XOR swizzle that makes the kernel's row-fragment loads bank-conflict
+//   free once a unit is copied linearly into shared memory; int8 radii rows are 64 bytes, linear.
+// * value codes at u_vcodes, stored as (code ^ 0x80) -- i.e. code + 128 as a byte -- in mma
+//   fragment order: token l = 16*kk + 8*a + 2*t + b (kk: 16-token step, a: upper/lower 8,
+//   t: lane quad column, b: pair bit) and channel d = 32*G + 4*g + 2*e_hi + e_lo sit at byte
+//   kk*2048 + G*512 + g*64 + t*16 + a*8 + e_hi*4 + e_lo*2 + b, so lane 4g+t of a warp finds its
+//   whole A fragment for group G of step kk in one 16-byte word.
+// * angle codes at u_codes: code_row bytes per token, level-1 codes then deep codes, each
+//   packed as the reference packs them (4-bit: even index in the low nibble; 2-bit: LSB first).
+// * value scales at u_vscales (float16, one per token and 32-channel group) at half index
 //   kk*64 + t*16 + a*8 + G*2 + b, so a lane reads (scale[tok][G], scale[tok+1][G]) pairs for its
 //   two token pairs with two 16-byte loads.
-__host__ __device__ __forceinline__ int radii_f16_offset(int l, int j) {  // bytes
+__host__ __device__ __forceinline__ int radii_f16_offset(int l, int j) {  // bytes, l < 32
   return l * 128 + ((((j >> 3) ^ (l & 7))) << 4) + (j & 7) * 2;
 }
-__host__ __device__ __forceinline__ int vcode_offset(int l, int d) {  // bytes
+__host__ __device__ __forceinline__ int vcode_offset(int l, int d) {  // bytes, l < 32
   const int kk = l >> 4, r = l & 15, a = r >> 3, t = (r >> 1) & 3, b = r & 1;
   const int G = d >> 5, g = (d >> 2) & 7, e_hi = (d >> 1) & 1, e_lo = d & 1;
   return kk * 2048 + G * 512 + g * 64 + t * 16 + a * 8 + e_hi * 4 + e_lo * 2 + b;
 }
-__host__ __device__ __forceinline__ int vscale_index(int l, int G) {  // halves
+__host__ __device__ __forceinline__ int vscale_index(int l, int G) {  // halves, l < 32
   const int kk = l >> 4, r = l & 15, a = r >> 3, t = (r >> 1) & 3, b = r & 1;
   return kk * 64 + t * 16 + a * 8 + G * 2 + b;
+}
+
+// Addresses of token l (0..63) of a page block `pg` (global or shared memory).
+template <class LAY>
+__host__ __device__ __forceinline__ uint8_t* unit_of(const LAY& L, uint8_t* pg, int l) {
+  return pg + (l >> 5) * L.unit_bytes;
+}
+template <class LAY>
+__host__ __device__ __forceinline__ __half* radius_f16_at(const LAY& L, uint8_t* pg, int l, int j) {
+  return reinterpret_cast<__half*>(unit_of(L, pg, l) + radii_f16_offset(l & 31, j));
+}
+template <class LAY>
+__host__ __device__ __forceinline__ int8_t* radius_i8_at(const LAY& L, uint8_t* pg, int l, int j) {
+  return reinterpret_cast<int8_t*>(unit_of(L, pg, l) + (l & 31) * kPairs + j);
+}
+template <class LAY>
+__host__ __device__ __forceinline__ uint8_t* codes_at(const LAY& L, uint8_t* pg, int l) {  // level-1 then deep
+  return unit_of(L, pg, l) + L.u_codes + (l & 31) * L.code_row;
+}
+template <class LAY>
+__host__ __device__ __forceinline__ uint8_t* vcode_at(const LAY& L, uint8_t* pg, int l, int d) {
+  return unit_of(L, pg, l) + L.u_vcodes + vcode_offset(l & 31, d);
+}
+template <class LAY>
+__host__ __device__ __forceinline__ __half* vscale_at(const LAY& L, uint8_t* pg, int l, int G) {
+  return reinterpret_cast<__half*>(unit_of(L, pg, l) + L.u_vscales) + vscale_index(l & 31, G);
 }
 
 // ----------------------------------------------------------------------------- device helpers
@@ -112,6 +188,10 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+// Invalidate a barrier with no pending arrivals or transactions, before initialising it again.
+__device__ __forceinline__ void mbar_inval(uint64_t* bar) {
+  asm volatile("mbarrier.inval.shared::cta.b64 [%0];\n" ::"r"(smem_u32(bar)) : "memory");
 }
 // Make barrier initialisation visible to the async proxy (bulk copies complete on it).
 __device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }

@@ -37,32 +37,46 @@ int make_layout(const tp_format& f, Layout* out) {
   L.l1_row = f.l1_bits == 8 ? L.l1_pairs : (L.l1_pairs + 1) / 2;
   const int per = 8 / f.deep_bits;
   L.deep_row = (L.deep_pairs + per - 1) / per;
+  L.code_row = L.l1_row + L.deep_row;
   L.radii_row = f.int8_radii ? kPairs : kPairs * 2;
-  L.radii_page = int64_t(kPage) * L.radii_row;
-  L.l1_page = int64_t(kPage) * L.l1_row;
-  L.deep_page = int64_t(kPage) * L.deep_row;
+  // Unit: radii | value codes | angle codes | value scales (every size a multiple of 32 bytes).
+  L.u_vcodes = kUnit * L.radii_row;
+  L.u_codes = L.u_vcodes + kVCodesUnit;
+  L.u_vscales = L.u_codes + kUnit * L.code_row;
+  L.unit_bytes = L.u_vscales + kVScalesUnit;
+  L.page_bytes = 2 * L.unit_bytes;
   *out = L;
   return TP_OK;
 }
 
-int validate_pool(const tp_page_pool* pool, Layout* L, bool keys) {
+int validate_pool(const tp_page_pool* pool, Layout* L) {
   if (!pool) return fail(TP_ERR_INVALID, "page pool is NULL");
   int st = make_layout(pool->fmt, L);
   if (st != TP_OK) return st;
   if (pool->num_kv_heads <= 0) return fail(TP_ERR_INVALID, "num_kv_heads must be positive");
   if (pool->page_capacity < 0) return fail(TP_ERR_INVALID, "page_capacity must be >= 0");
   if (pool->page_capacity > 0) {
-    if (!pool->v_codes || !pool->v_scales) return fail(TP_ERR_INVALID, "page pool has a NULL value field");
+    if (!pool->pages) return fail(TP_ERR_INVALID, "page pool has NULL pages");
+    if (reinterpret_cast<uintptr_t>(pool->pages) & 15) return fail(TP_ERR_INVALID, "page pool must be 16-byte aligned");
+    if (pool->fmt.int8_radii && !pool->radii_scales) return fail(TP_ERR_INVALID, "int8 radii require radii_scales");
+  }
+  return TP_OK;
+}
+
+int validate_store(const tp_block_store* ref, Layout* L, bool keys) {
+  if (!ref) return fail(TP_ERR_INVALID, "block store is NULL");
+  int st = make_layout(ref->fmt, L);
+  if (st != TP_OK) return st;
+  if (ref->num_kv_heads <= 0) return fail(TP_ERR_INVALID, "num_kv_heads must be positive");
+  if (ref->page_capacity < 0) return fail(TP_ERR_INVALID, "page_capacity must be >= 0");
+  if (ref->page_capacity > 0) {
+    if (!ref->v_codes || !ref->v_scales) return fail(TP_ERR_INVALID, "block store has a NULL value field");
     if (keys) {
-      if (!pool->radii) return fail(TP_ERR_INVALID, "page pool has NULL radii");
-      if (L->l1_row > 0 && !pool->angle_codes_l1) return fail(TP_ERR_INVALID, "angle_codes_l1 is NULL");
-      if (L->deep_row > 0 && !pool->angle_codes_deep) return fail(TP_ERR_INVALID, "angle_codes_deep is NULL");
-      if (pool->fmt.int8_radii && !pool->radii_scales) return fail(TP_ERR_INVALID, "int8 radii require radii_scales");
+      if (!ref->radii) return fail(TP_ERR_INVALID, "block store has NULL radii");
+      if (L->l1_row > 0 && !ref->angle_codes_l1) return fail(TP_ERR_INVALID, "angle_codes_l1 is NULL");
+      if (L->deep_row > 0 && !ref->angle_codes_deep) return fail(TP_ERR_INVALID, "angle_codes_deep is NULL");
+      if (ref->fmt.int8_radii && !ref->radii_scales) return fail(TP_ERR_INVALID, "int8 radii require radii_scales");
     }
-    const void* ptrs[] = {pool->radii, pool->angle_codes_l1, pool->angle_codes_deep, pool->v_codes, pool->v_scales};
-    for (const void* q : ptrs)
-      if (q && (reinterpret_cast<uintptr_t>(q) & 15))
-        return fail(TP_ERR_INVALID, "page pool fields must be 16-byte aligned");
   }
   return TP_OK;
 }
@@ -73,12 +87,13 @@ __global__ void __launch_bounds__(256) encode_pages_kernel(PoolArgs P, const T* 
                                                            int n_pages, int32_t* d_state) {
   __shared__ uint8_t s_codes[kPage * kPairs];
   __shared__ float s_red[8];
-  __shared__ __align__(16) uint8_t s_v[kVCodesPage];
-  __shared__ __align__(16) __half s_scales[kPage * 4];
+  __shared__ __align__(16) uint8_t s_page[kMaxPageBytes];
+  __shared__ __half s_rscale;
   const int p = blockIdx.x, h = blockIdx.y;
   const int64_t tok0 = src_token0 + int64_t(p) * kPage;
   encode_page<T>(k + h * head_stride + tok0 * token_stride, v + h * head_stride + tok0 * token_stride, token_stride,
-                 P.page(h, dst_page + p), P, s_codes, s_red, s_v, s_scales);
+                 P, s_page, &s_rscale, s_codes, s_red);
+  store_page_block(P, s_page, s_rscale, h, dst_page + p);
   if (d_state) {
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -100,8 +115,8 @@ __global__ void __launch_bounds__(256) append_kernel(PoolArgs P, T* tail_k, T* t
                                                      int n_tokens) {
   __shared__ uint8_t s_codes[kPage * kPairs];
   __shared__ float s_red[8];
-  __shared__ __align__(16) uint8_t s_v[kVCodesPage];
-  __shared__ __align__(16) __half s_scales[kPage * 4];
+  __shared__ __align__(16) uint8_t s_page[kMaxPageBytes];
+  __shared__ __half s_rscale;
   const int h = blockIdx.x;
   const int n_pages = d_state[0], tail_len = d_state[1];
   const bool overflow = tail_len < 0 || tail_len + n_tokens > kPage;
@@ -121,7 +136,8 @@ __global__ void __launch_bounds__(256) append_kernel(PoolArgs P, T* tail_k, T* t
   }
   __syncthreads();
   if (fills) {
-    encode_page<T>(tk, tv, kD, P.page(h, n_pages), P, s_codes, s_red, s_v, s_scales);
+    encode_page<T>(tk, tv, kD, P, s_page, &s_rscale, s_codes, s_red);
+    store_page_block(P, s_page, s_rscale, h, n_pages);
     __syncthreads();
   }
   if (threadIdx.x == 0) {
@@ -144,7 +160,7 @@ extern "C" {
 
 const char* tp_last_error(void) { return g_last_error.c_str(); }
 
-int tp_version(void) { return 1; }
+int tp_version(void) { return 2; }
 
 int tp_row_bytes(const tp_format* fmt, int32_t* l1_row_bytes, int32_t* deep_row_bytes) {
   if (!fmt) return fail(TP_ERR_INVALID, "format is NULL");
@@ -153,6 +169,15 @@ int tp_row_bytes(const tp_format* fmt, int32_t* l1_row_bytes, int32_t* deep_row_
   if (st != TP_OK) return st;
   if (l1_row_bytes) *l1_row_bytes = L.l1_row;
   if (deep_row_bytes) *deep_row_bytes = L.deep_row;
+  return TP_OK;
+}
+
+int tp_unit_bytes(const tp_format* fmt, int32_t* unit_bytes) {
+  if (!fmt) return fail(TP_ERR_INVALID, "format is NULL");
+  Layout L;
+  int st = make_layout(*fmt, &L);
+  if (st != TP_OK) return st;
+  if (unit_bytes) *unit_bytes = L.unit_bytes;
   return TP_OK;
 }
 
