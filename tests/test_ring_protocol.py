@@ -16,28 +16,31 @@ import pytest
 
 
 class _Bar:
-    def __init__(self):
-        self.ph, self.arrived, self.tx = 0, False, False
+    def __init__(self, count=1):
+        self.ph, self.count, self.arrived, self.tx = 0, count, 0, 0
 
     def done(self, parity):  # try_wait.parity: the phase of that parity has completed
         return (self.ph & 1) != parity
 
-    def arrive(self):
-        assert not self.arrived, "second arrival in one phase"
-        self.arrived = True
+    def arrive(self, tx=0):
+        assert self.arrived < self.count, "more arrivals than the barrier's count in one phase"
+        self.arrived += 1
+        self.tx += tx
         self.settle()
 
     def settle(self):
-        if self.arrived and not self.tx:
-            self.ph, self.arrived = self.ph + 1, False
+        if self.arrived == self.count and self.tx == 0:
+            self.ph, self.arrived = self.ph + 1, 0
 
 
-def _simulate(n, C, S, NP, seed, owned=True, R=None):
+def _simulate(n, C, S, NP, seed, owned=True, R=None, split=1):
+    """C consumers with S stages each; NP issuing lanes (owned=False: stage k % R, lane k % NP);
+    with `split`, lanes split * w .. split * w + split - 1 each copy one part of consumer w's units."""
     rng = random.Random(seed)
     R = R or C * S
-    full = [_Bar() for _ in range(R)]
+    full = [_Bar(split) for _ in range(R)]
     empty = [_Bar() for _ in range(R)]
-    data, inflight = [None] * R, []
+    data, inflight = [[None] * split for _ in range(R)], []
 
     def stage_of(k):
         if owned:
@@ -45,19 +48,21 @@ def _simulate(n, C, S, NP, seed, owned=True, R=None):
             return w * S + j % S, j // S
         return k % R, k // R
 
-    def issue(k):
+    def issue(k, part=0):
         slot, wrap = stage_of(k)
         if wrap > 0:
             while not empty[slot].done((wrap - 1) & 1):
                 yield
-        assert not full[slot].arrived, "issue into a stage whose copy is pending"
-        full[slot].tx = True
-        full[slot].arrive()
-        inflight.append((slot, k))
+        full[slot].arrive(tx=1)
+        inflight.append((slot, part, k))
         yield
 
     def producer(p):
-        if owned:
+        if owned and split > 1:
+            w, part = divmod(p, split)
+            for k in range(w, n, C):
+                yield from issue(k, part)
+        elif owned:
             for j in range((n + C - 1) // C):
                 for w in range(p, C, NP):
                     if w + C * j < n:
@@ -71,19 +76,20 @@ def _simulate(n, C, S, NP, seed, owned=True, R=None):
             slot, wrap = stage_of(k)
             while not full[slot].done(wrap & 1):
                 yield
-            assert data[slot] == k, f"read unit {data[slot]} expecting {k}"
+            assert all(d == k for d in data[slot]), f"read units {data[slot]} expecting {k}"
             yield
             empty[slot].arrive()
 
-    alive = [producer(p) for p in range(NP)] + [consumer(w) for w in range(C)]
+    lanes = C * split if split > 1 else NP
+    alive = [producer(p) for p in range(lanes)] + [consumer(w) for w in range(C)]
     steps = 0
     while alive or inflight:
         steps += 1
         assert steps < 10 ** 6, "no progress"
         if inflight and rng.random() < 0.3:
-            slot, k = inflight.pop(rng.randrange(len(inflight)))
-            data[slot] = k
-            full[slot].tx = False
+            slot, part, k = inflight.pop(rng.randrange(len(inflight)))
+            data[slot][part] = k
+            full[slot].tx -= 1
             full[slot].settle()
             continue
         if alive:
@@ -100,6 +106,13 @@ def test_owned_stages_never_alias(C, S, NP):
     for n in (1, C - 1, C + 1, 55, 221):
         for seed in range(8):
             _simulate(max(n, 1), C, S, NP, seed)
+
+
+@pytest.mark.parametrize("split", [2, 4])
+def test_split_copies_never_alias(split):
+    for n in (1, 6, 8, 55, 221):
+        for seed in range(8):
+            _simulate(n, 7, 2, 0, seed, split=split)
 
 
 def test_shared_ring_aliases():

@@ -39,19 +39,16 @@
 
 namespace tp {
 
-#ifndef TP_PRODUCER_WARPS
-#define TP_PRODUCER_WARPS 1
-#endif
-#ifndef TP_PRODUCER_LANES
-#define TP_PRODUCER_LANES 8
-#endif
 #ifndef TP_CONSUMERS
 #define TP_CONSUMERS 7
 #endif
+#ifndef TP_COPY_SPLIT
+#define TP_COPY_SPLIT 1
+#endif
 constexpr int kConsumers = TP_CONSUMERS;             // page-pass compute warps
-constexpr int kProducerWarps = TP_PRODUCER_WARPS;    // page-pass copy warps
-constexpr int kProducerLanes = TP_PRODUCER_LANES;    // issuing lanes per copy warp
-constexpr int kProducers = kProducerWarps * kProducerLanes;
+constexpr int kCopySplit = TP_COPY_SPLIT;            // copy-warp lanes (and bulk copies) per unit
+constexpr int kIssuers = kConsumers * kCopySplit;    // issuing lanes of the copy warp(s)
+constexpr int kProducerWarps = (kIssuers + 31) / 32;
 constexpr int kThreads = (kConsumers + kProducerWarps) * 32;
 constexpr int kMaxStages = 24;                   // ring stages (one unit each)
 constexpr int kMaxHeads = 8;  // query heads per unit (N of the mma)
@@ -98,6 +95,7 @@ struct AttnParams {
   int smem_bar_off, smem_lut_off, smem_merge_off, smem_stage_off;
   int n_stages;  // ring stages of the page pass
   uint32_t lut[2 * kLutEntries];  // half2 (cos, sin) per code: level-1 [0, 256), deep [256, 512)
+  int lut_deep;                   // shared-memory copy: level-1 entries, then deep from here
 };
 
 // Work partition: the U units (half pages, head-major, uph per head) are cut into C = min(U,
@@ -248,7 +246,7 @@ __device__ __forceinline__ void decode_row_general(const uint8_t* stage, const A
       if (P.deep_bits == 8) code = deeprow[rel];
       else if (P.deep_bits == 4) code = (deeprow[rel >> 1] >> (4 * (rel & 1))) & 15u;
       else code = (deeprow[rel >> 2] >> (2 * (rel & 3))) & 3u;
-      cs = lut[kLutEntries + code];
+      cs = lut[P.lut_deep + code];
     }
     float rad;
     if (P.int8_radii) {
@@ -323,11 +321,14 @@ __device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, c
 // Unit `half` of page `page` of KV head kvh into a stage: one bulk copy (every unit is
 // contiguous in the pool) completing on the stage's mbarrier.
 __device__ __forceinline__ void issue_half(uint8_t* stage, uint64_t* bar, const AttnParams& P, int kvh, int page,
-                                           int half, uint64_t pol) {
+                                           int half, int part, uint64_t pol) {
   const int64_t unit = (int64_t(kvh) * P.page_capacity + page) * 2 + half;
+  const int chunk = (P.unit_bytes / kCopySplit + 15) & ~15;
+  const int off = min(part * chunk, P.unit_bytes);
+  const uint32_t bytes = uint32_t(min(chunk, P.unit_bytes - off));
   fence_proxy_async_smem();
-  mbar_arrive_expect_tx(bar, uint32_t(P.unit_bytes));
-  bulk_g2s_hint(stage, P.pages + unit * P.unit_bytes, uint32_t(P.unit_bytes), bar, pol);
+  mbar_arrive_expect_tx(bar, bytes);
+  if (bytes) bulk_g2s_hint(stage + off, P.pages + unit * P.unit_bytes + off, bytes, bar, pol);
 }
 
 // Bounded wait for phase `parity` of a stage barrier (about a second); false on timeout.
@@ -462,11 +463,12 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity) { retu
 // Consumer w takes CTA units w, w + kConsumers, ... and owns ring stages [w*S, w*S + S)
 // (S = P.n_stages / kConsumers), its j-th unit in stage w*S + j % S; each stage has a "full"
 // mbarrier (the bulk copy of a unit completes on it) and an "empty" one (the consumer releases
-// the stage).  Issuing lane p (lane i of producer warp v, p = v*kProducerLanes + i) serves the
-// consumers w = p (mod kProducers), their j-th units in turn, waiting for a stage's release
-// before reusing it.  Every stage has one producer and one consumer, so a wait is never more
-// than one phase ahead of its barrier.  A thread dispatches one bulk copy at a time, so the
-// copies are spread over several issuing lanes and never hold up the warps that compute;
+// the stage).  Issuing lane p of the copy warp(s) serves consumer p / kCopySplit: it issues
+// part p % kCopySplit of each of that consumer's units in turn (one bulk copy; the stage's
+// full barrier expects kCopySplit arrivals), waiting for the stage's release before reusing
+// it.  Every stage is filled and drained by fixed threads that follow its phases in order, so
+// no wait is ever more than one phase ahead of its barrier.  A thread dispatches one bulk copy
+// at a time, so the copies are spread over lanes that never hold up the warps that compute;
 // consumers get the same number of units to within one.
 template <bool kFast>
 __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __grid_constant__ AttnParams P) {
@@ -482,8 +484,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   const int gmax = P.gmax;
   const int rec_stride = gmax * TP_PARTIAL_FLOATS;
   const bool producer = warp >= kConsumers;
-  const int pw = (warp - kConsumers) * kProducerLanes + lane;  // issuing-lane index
-  const bool issuer = producer && lane < kProducerLanes;
+  const int pw = (warp - kConsumers) * 32 + lane;  // issuing-lane index
+  const bool issuer = producer && pw < kIssuers;
+  const int pcons = pw / kCopySplit, ppart = pw % kCopySplit;  // the consumer and part it serves
   const int c = blockIdx.x;
   const uint64_t pol = l2_evict_first_policy();
 
@@ -493,13 +496,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   {
     const int n1 = 1 << P.l1_bits, n2 = 1 << P.deep_bits;
     for (int i = tid; i < n1 + n2; i += kThreads) {
-      const int j = i < n1 ? i : kLutEntries + (i - n1);
-      lut[j] = P.lut[j];
+      lut[i] = P.lut[i < n1 ? i : kLutEntries + (i - n1)];
     }
   }
   auto init_barriers = [&]() {
     for (int st = 0; st < R; ++st) {
-      mbar_init(&full[st], 1);
+      mbar_init(&full[st], kCopySplit);
       mbar_init(&empty[st], 1);
     }
     fence_mbar_init();
@@ -520,19 +522,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
       return;
     }
     const int3 u = unit_ref(pt, w + kConsumers * j);
-    issue_half(ring + slot * P.stage_bytes, &full[slot], P, (pt.vh_first + u.x) / P.nqc, u.y, u.z, pol);
+    issue_half(ring + slot * P.stage_bytes, &full[slot], P, (pt.vh_first + u.x) / P.nqc, u.y, u.z, ppart, pol);
   };
-  // Units [j0, j1) of every consumer this lane serves, round by round.
+  // Units [j0, j1) of the consumer this lane serves.
   auto produce_range = [&](int j0, int j1) {
-    for (int j = j0; j < j1; ++j) {
-      bool any = false;
-      for (int w = pw; w < kConsumers && !timed_out; w += kProducers) {
-        if (w + kConsumers * j >= pt.n) continue;
-        any = true;
-        produce(w, j);
-      }
-      if (!any || timed_out) break;
-    }
+    for (int j = j0; j < j1 && pcons + kConsumers * j < pt.n && !timed_out; ++j) produce(pcons, j);
   };
   // Each consumer's first S units go in flight now, on the partition of the page count read
   // now.  Every page below the newest one was written by a launch that had completed before
@@ -553,8 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
     // barriers and start again on the new partition.
     if (early && issuer) {
       for (int j = 0; j < S; ++j)
-        for (int w = pw; w < kConsumers; w += kProducers)
-          if (w + kConsumers * j < pt.n && !stage_wait(&full[w * S + j], 0)) timed_out = true;
+        if (pcons + kConsumers * j < pt.n && !stage_wait(&full[pcons * S + j], 0)) timed_out = true;
     }
     __syncthreads();
     if (tid == 0) {
@@ -1153,25 +1146,26 @@ static int num_sms() {
   return g_num_sms;
 }
 
-// Dynamic shared memory the page pass may use: the opt-in per-block limit, and no more than
-// leaves room on one SM for a split-combine CTA beside it.
+// Dynamic shared memory the page pass may use: the opt-in per-block limit and, when the
+// registers allow a split-combine CTA beside a page-pass CTA on one SM (so it starts, and
+// finishes the dense tail, while the page pass runs), no more than leaves room for it.
 static int ring_budget(const void* page_pass) {
   static int budget = 0;
   if (budget == 0) {
-    int dev = 0, per_sm = 233472, per_block = 232448, reserved = 1024;
+    int dev = 0, per_sm = 233472, per_block = 232448, reserved = 1024, regs = 65536;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
     cudaDeviceGetAttribute(&per_block, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    cudaDeviceGetAttribute(&regs, cudaDevAttrMaxRegistersPerMultiprocessor, dev);
     cudaFuncAttributes comb = {}, pp = {};
     cudaFuncGetAttributes(&comb, reinterpret_cast<const void*>(split_combine_kernel));
     cudaFuncGetAttributes(&pp, page_pass);
-#ifdef EXP_FULL_RING
+    auto up8 = [](int r) { return (r + 7) / 8 * 8; };
+    const bool beside = up8(pp.numRegs) * kThreads + up8(comb.numRegs) * kCombineThreads <= regs;
     budget = per_block - int(pp.sharedSizeBytes) - 256;
-#else
-    budget = min(per_block - int(pp.sharedSizeBytes),
-                 per_sm - 2 * reserved - int(comb.sharedSizeBytes) - int(pp.sharedSizeBytes)) - 256;
-#endif
+    if (beside)
+      budget = min(budget, per_sm - 2 * reserved - int(comb.sharedSizeBytes) - int(pp.sharedSizeBytes) - 256);
   }
   return budget;
 }
@@ -1294,7 +1288,8 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
   const int merge_bytes = kConsumers * P.gmax * TP_PARTIAL_FLOATS * int(sizeof(float));
   P.smem_bar_off = 0;                       // full and empty barrier per ring stage
   P.smem_lut_off = up(2 * kMaxStages * 8, 128);
-  P.smem_merge_off = P.smem_lut_off + 2 * kLutEntries * 4;
+  P.lut_deep = 1 << P.l1_bits;
+  P.smem_merge_off = P.smem_lut_off + up(4 * ((1 << P.l1_bits) + (1 << P.deep_bits)), 128);
   P.smem_stage_off = up(P.smem_merge_off + merge_bytes, 128);
 
   const bool fast = P.l1_bits == 4 && P.deep_bits == 4 && pool->fmt.split_dim == 64 && !P.int8_radii;
