@@ -853,23 +853,25 @@ __device__ __noinline__ float3 flush_partial(const AttnParams& P, CombineSmem& s
 }
 
 // ----------------------------------------------------------------------------- cross-GPU exchange
-// Exchange buffer of one rank: records [world][H_q][kRecFloats] written by every rank into
-// every rank's buffer (peer stores over NVLink), flags [world][H_q] (the epoch of the record a
-// rank last published there), then this rank's epoch word and ticket.
-__host__ __device__ inline size_t x_flags_off(int world, int hq) {
-  return (size_t(world) * hq * kRecFloats * sizeof(float) + 255) & ~size_t(255);
-}
+// Exchange buffer of one rank: records [world][H_q][kExchWords] of 64-bit words written by every
+// rank into every rank's buffer (peer stores over NVLink), then this rank's epoch word and
+// ticket.  A word holds one float of a record (m, l, o[128]) in its low half and the call's
+// epoch in its high half, so a reader knows a word is current from the word alone: an
+// aligned 64-bit store is single-copy atomic, and no fence or flag is needed between the
+// data and its validity (one one-way NVLink trip instead of store, release fence, flag store).
+constexpr int kExchWords = TP_PARTIAL_FLOATS;
 __host__ __device__ inline size_t x_epoch_off(int world, int hq) {
-  return (x_flags_off(world, hq) + size_t(world) * hq * sizeof(int) + 255) & ~size_t(255);
+  return (size_t(world) * hq * kExchWords * sizeof(uint64_t) + 255) & ~size_t(255);
 }
 
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_word_sys(uint64_t* p, float v, uint32_t epoch) {
+  const uint64_t w = uint64_t(__float_as_uint(v)) | (uint64_t(epoch) << 32);
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;\n" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ uint64_t ld_word_sys(const uint64_t* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];\n" : "=l"(w) : "l"(p) : "memory");
+  return w;
 }
 
 // Publish this rank's merged (m, l, o) of query head qh to every rank, wait (bounded) until
@@ -878,47 +880,64 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
 __device__ __forceinline__ bool exchange_merge(const AttnParams& P, int qh, int epoch, float& M, float& L, float& O) {
   const int tid = threadIdx.x;
   const int W = P.xworld, hq = P.num_q_heads;
-  for (int r = 0; r < W; ++r) {
-    float* rec = reinterpret_cast<float*>(P.xbuf[r]) + (size_t(P.xrank) * hq + qh) * kRecFloats;
-    if (tid < kD) rec[2 + tid] = O;
-    if (tid == 0) { rec[0] = M; rec[1] = L; }
-  }
-  // The barrier orders every thread's record stores before the flag stores, which release
-  // them at system scope (the peers read them over NVLink).
-  __syncthreads();
-  if (tid < W) st_release_sys(reinterpret_cast<int*>(P.xbuf[tid] + x_flags_off(W, hq)) + P.xrank * hq + qh, epoch);
-  __shared__ int s_ok;
-  if (tid == 0) s_ok = 1;
-  __syncthreads();
-  if (tid < W) {
-    const int* f = reinterpret_cast<const int*>(P.xbuf[P.xrank] + x_flags_off(W, hq)) + tid * hq + qh;
-    const long long t0 = clock64();
-    while (ld_acquire_sys(f) != epoch) {
-      if (clock64() - t0 > (1ll << 31)) {
-        s_ok = 0;
-        break;
+  const uint32_t ep = uint32_t(epoch);
+  if (tid < kD) {
+    for (int r = 0; r < W; ++r) {
+      uint64_t* rec = reinterpret_cast<uint64_t*>(P.xbuf[r]) + (size_t(P.xrank) * hq + qh) * kExchWords;
+      st_word_sys(rec + 2 + tid, O, ep);
+      if (tid == 0) {
+        st_word_sys(rec, M, ep);
+        st_word_sys(rec + 1, L, ep);
       }
     }
   }
+  __shared__ int s_ok;
+  if (tid == 0) s_ok = 1;
   __syncthreads();
   if (tid < kD) {
-    const float* base = reinterpret_cast<const float*>(P.xbuf[P.xrank]) + size_t(qh) * kRecFloats;
+    // Each thread reads the (m, l, o[tid]) words of every rank's record once they carry this
+    // epoch (m first: the merge needs the maximum before the weights).
+    const uint64_t* base = reinterpret_cast<const uint64_t*>(P.xbuf[P.xrank]) + size_t(qh) * kExchWords;
+    float m[TP_MAX_RANKS], l[TP_MAX_RANKS], o[TP_MAX_RANKS];
+    bool ok = true;
+    const long long t0 = clock64();
+#pragma unroll
+    for (int r = 0; r < TP_MAX_RANKS; ++r) {
+      m[r] = -INFINITY;
+      l[r] = o[r] = 0.f;
+      if (r < W && ok) {
+        const uint64_t* rec = base + size_t(r) * hq * kExchWords;
+        uint64_t wm, wl, wo;
+        while (true) {
+          wm = ld_word_sys(rec);
+          wl = ld_word_sys(rec + 1);
+          wo = ld_word_sys(rec + 2 + tid);
+          if (uint32_t(wm >> 32) == ep && uint32_t(wl >> 32) == ep && uint32_t(wo >> 32) == ep) break;
+          if (clock64() - t0 > (1ll << 31)) { ok = false; break; }
+        }
+        m[r] = __uint_as_float(uint32_t(wm));
+        l[r] = __uint_as_float(uint32_t(wl));
+        o[r] = __uint_as_float(uint32_t(wo));
+      }
+    }
+    if (!ok) s_ok = 0;
     float Mx = -INFINITY;
-    for (int r = 0; r < W; ++r) Mx = fmaxf(Mx, __ldcv(base + size_t(r) * hq * kRecFloats));
+#pragma unroll
+    for (int r = 0; r < TP_MAX_RANKS; ++r) Mx = fmaxf(Mx, m[r]);
     float Lx = 0.f, Ox = 0.f;
-    if (Mx != -INFINITY) {
-      for (int r = 0; r < W; ++r) {
-        const float* rec = base + size_t(r) * hq * kRecFloats;
-        const float m = __ldcv(rec);
-        const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - Mx);
-        Lx = fmaf(__ldcv(rec + 1), w, Lx);
-        Ox = fmaf(__ldcv(rec + 2 + tid), w, Ox);
+    if (ok && Mx != -INFINITY) {
+#pragma unroll
+      for (int r = 0; r < TP_MAX_RANKS; ++r) {
+        const float w = (m[r] == -INFINITY) ? 0.f : exp2_approx(m[r] - Mx);
+        Lx = fmaf(l[r], w, Lx);
+        Ox = fmaf(o[r], w, Ox);
       }
     }
     M = Mx;
     L = Lx;
     O = Ox;
   }
+  __syncthreads();
   return s_ok != 0;
 }
 
