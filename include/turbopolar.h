@@ -210,9 +210,11 @@ int tp_combine_partials(const float* partials, int32_t n_parts, int32_t num_q_he
 /* ---- Sequence sharding over the GPUs of one node, merged inside the attention launch.
  * No reference counterpart (the reference runs on one device).  Every rank holds a contiguous
  * page range of every KV head; its attention launch publishes each query head's partial
- * (m, l, o) into every rank's exchange buffer with peer stores over NVLink, raises a flag
- * there, waits (bounded, about a second) for all ranks' records of that head and merges them,
- * so each rank writes the whole fp16 output with no collective library call.  All ranks must
+ * (m, l, o) into every rank's exchange buffer with peer stores over NVLink, as 64-bit words
+ * that each carry one value and the call's epoch, waits (bounded, about a second) until every
+ * rank's words of that head carry the epoch and merges them, so each rank writes the whole
+ * fp16 output with no collective library call (tp_exchange_bytes sizes a buffer; allocate it
+ * zero-filled, as tp_ipc_alloc does).  All ranks must
  * make the same sequence of sharded calls on their buffers (the buffers' epoch words advance
  * once per call).  A wait that runs out leaves workspace word 0 = 3 (the output is unusable). */
 #define TP_MAX_RANKS 8

@@ -8,7 +8,8 @@ partials are merged with ``M = max m_r, L = sum l_r 2^(m_r-M), O = sum o_r 2^(m_
 
 Two exchanges: ``PeerExchange`` (the default) does it inside the attention launch -- every
 rank's split-combine CTAs store their records into every rank's buffer over NVLink (buffers
-mapped through CUDA IPC), raise a flag, wait (bounded) for the other ranks' records and merge;
+mapped through CUDA IPC) as 64-bit words carrying the call's epoch, wait (bounded) until the
+other ranks' words carry it and merge;
 the NCCL path (``exchange=False``) writes ``partial_out``, all-gathers it and runs
 ``tp_combine_partials``.
 """
