@@ -93,6 +93,8 @@ struct AttnParams {
   int* ws_error;
   int stage_bytes, off_vcodes, off_codes, off_vscales;  // a stage holds one unit as laid out in the pool
   int smem_bar_off, smem_lut_off, smem_merge_off, smem_stage_off;
+  int smem_scale_off;  // float radius scale of the unit in each ring stage (int8 radii)
+  int smem_rlut_off;   // per compute warp: float16 exp(code * scale) for the 256 int8 codes
   int n_stages;  // ring stages of the page pass
   uint32_t lut[2 * kLutEntries];  // half2 (cos, sin) per code: level-1 [0, 256), deep [256, 512)
   int lut_deep;                   // shared-memory copy: level-1 entries, then deep from here
@@ -260,18 +262,43 @@ __device__ __forceinline__ void decode_row_general(const uint8_t* stage, const A
   }
 }
 
+// Adapter path: log-int8 radii, split_dim 0 and 8-bit angle codes (the format the Llama
+// adapter uses, benchmarks/turbopolar_fast_attention.py:217-228).  rlut holds float16
+// exp(c * scale) for the 256 int8 codes of this unit's page (index c + 128).
+__device__ __forceinline__ void decode_row_adapter(const uint8_t* stage, const AttnParams& P, const uint32_t* lut,
+                                                   const __half* rlut, int r, int t, uint32_t (&kp)[16]) {
+  const uint4 R = lds128(stage + r * kPairs + 16 * t);
+  const uint4 C = lds128(stage + P.off_codes + r * kPairs + 16 * t);
+  const uint32_t rw[4] = {R.x, R.y, R.z, R.w}, cw[4] = {C.x, C.y, C.z, C.w};
+  const uint32_t* dl = lut + P.lut_deep;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t rb = (rw[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+    const uint32_t cb = (cw[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+    kp[i] = h2_as_u32(__hmul2(__half2half2(rlut[rb ^ 0x80u]), u32_as_h2(dl[cb])));
+  }
+}
+
+// Key decode of a page pass: the general path (any format), the table-driven default format,
+// and the adapter format.
+enum { kModeGeneral = 0, kModeFast = 1, kModeAdapter = 2 };
+
 // ----------------------------------------------------------------------------- one half page
-template <bool kFast>
+template <int kMode>
 __device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, const AttnParams& P, const uint32_t* lut,
-                                             const uint32_t (&qf)[16], float radius_scale, int valid_tokens, int lane) {
+                                             const __half* rlut, const uint32_t (&qf)[16], float radius_scale,
+                                             int valid_tokens, int lane) {
   const int g = lane >> 2, t = lane & 3;
   float sc[2][4];
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt) {
     uint32_t k0[16], k1[16];
-    if (kFast) {
+    if (kMode == kModeFast) {
       decode_row_fast(stage, P, lut, 16 * mt + g, t, k0);
       decode_row_fast(stage, P, lut, 16 * mt + g + 8, t, k1);
+    } else if (kMode == kModeAdapter) {
+      decode_row_adapter(stage, P, lut, rlut, 16 * mt + g, t, k0);
+      decode_row_adapter(stage, P, lut, rlut, 16 * mt + g + 8, t, k1);
     } else {
       decode_row_general(stage, P, lut, radius_scale, 16 * mt + g, t, k0);
       decode_row_general(stage, P, lut, radius_scale, 16 * mt + g + 8, t, k1);
@@ -470,7 +497,7 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity) { retu
 // no wait is ever more than one phase ahead of its barrier.  A thread dispatches one bulk copy
 // at a time, so the copies are spread over lanes that never hold up the warps that compute;
 // consumers get the same number of units to within one.
-template <bool kFast>
+template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __grid_constant__ AttnParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ tp_state s_pre;  // cache state as read before the wait, one read for the CTA
@@ -479,6 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.smem_bar_off);
   uint64_t* empty = full + kMaxStages;
   uint8_t* ring = smem + P.smem_stage_off;
+  float* stage_scale = reinterpret_cast<float*>(smem + P.smem_scale_off);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int R = P.n_stages, S = R / kConsumers;
   const int gmax = P.gmax;
@@ -522,7 +550,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
       return;
     }
     const int3 u = unit_ref(pt, w + kConsumers * j);
-    issue_half(ring + slot * P.stage_bytes, &full[slot], P, (pt.vh_first + u.x) / P.nqc, u.y, u.z, ppart, pol);
+    const int kvh = (pt.vh_first + u.x) / P.nqc;
+    // The unit's radius scale travels beside its copy: stored before the arrival on the
+    // stage's full barrier, which releases it to the consumer.
+    if (P.int8_radii && ppart == 0)
+      stage_scale[slot] = __half2float(P.radii_scales[int64_t(kvh) * P.page_capacity + u.y]);
+    issue_half(ring + slot * P.stage_bytes, &full[slot], P, kvh, u.y, u.z, ppart, pol);
   };
   // Units [j0, j1) of the consumer this lane serves.
   auto produce_range = [&](int j0, int j1) {
@@ -575,6 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   } else {
     WarpAcc A;
     uint32_t qf[16];
+    __half* rlut = reinterpret_cast<__half*>(smem + P.smem_rlut_off) + warp * 256;
     int cur = -1;        // segment of the accumulator (-1: none yet)
     int kvh = 0, gc = gmax;
     // Ring stage and phase of this warp's next unit.
@@ -596,9 +630,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
       if (ready) {
         const int64_t pos0 = (int64_t(st.first_page) + u.y) * kPage + u.z * kHalf;
         const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, kHalf));
-        float rs = 0.f;
-        if (P.int8_radii) rs = __half2float(P.radii_scales[int64_t(kvh) * P.page_capacity + u.y]);
-        process_half<kFast>(A, ring + slot * P.stage_bytes, P, lut, qf, rs, vt, lane);
+        const float rs = P.int8_radii ? stage_scale[slot] : 0.f;
+        if (kMode == kModeAdapter) {
+          // float16 exp(c * scale) of every int8 code c of this unit's page (decoder.py:57-63);
+          // the previous unit's reads of the table ended at the __syncwarp that closed it.
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int cidx = lane + 32 * k;
+            rlut[cidx] = __float2half_rn(__expf(float(cidx - 128) * rs));
+          }
+          __syncwarp();
+        }
+        process_half<kMode>(A, ring + slot * P.stage_bytes, P, lut, rlut, qf, rs, vt, lane);
       } else {
         timed_out = true;  // the unit is left out; the error word marks the result unusable
       }
@@ -1169,7 +1212,15 @@ static int num_sms() {
 // registers allow a split-combine CTA beside a page-pass CTA on one SM (so it starts, and
 // finishes the dense tail, while the page pass runs), no more than leaves room for it.
 static int ring_budget(const void* page_pass) {
-  static int budget = 0;
+  static const void* fns[4] = {};
+  static int budgets[4] = {};
+  int slot = 0;
+  while (slot < 3 && fns[slot] && fns[slot] != page_pass) ++slot;
+  int& budget = budgets[slot];
+  if (fns[slot] != page_pass) {
+    fns[slot] = page_pass;
+    budget = 0;
+  }
   if (budget == 0) {
     int dev = 0, per_sm = 233472, per_block = 232448, reserved = 1024, regs = 65536;
     cudaGetDevice(&dev);
@@ -1309,12 +1360,17 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
   P.smem_lut_off = up(2 * kMaxStages * 8, 128);
   P.lut_deep = 1 << P.l1_bits;
   P.smem_merge_off = P.smem_lut_off + up(4 * ((1 << P.l1_bits) + (1 << P.deep_bits)), 128);
-  P.smem_stage_off = up(P.smem_merge_off + merge_bytes, 128);
+  P.smem_scale_off = up(P.smem_merge_off + merge_bytes, 128);
+  P.smem_rlut_off = P.smem_scale_off + up(kMaxStages * 4, 128);
+  const int mode = (P.l1_bits == 4 && P.deep_bits == 4 && pool->fmt.split_dim == 64 && !P.int8_radii) ? kModeFast
+                   : (P.int8_radii && pool->fmt.split_dim == 0 && P.deep_bits == 8)                 ? kModeAdapter
+                                                                                                   : kModeGeneral;
+  P.smem_stage_off = up(P.smem_rlut_off + (mode == kModeAdapter ? kConsumers * 256 * 2 : 0), 128);
 
-  const bool fast = P.l1_bits == 4 && P.deep_bits == 4 && pool->fmt.split_dim == 64 && !P.int8_radii;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const void* fn = fast ? reinterpret_cast<const void*>(decode_attention_kernel<true>)
-                        : reinterpret_cast<const void*>(decode_attention_kernel<false>);
+  const void* fn = mode == kModeFast      ? reinterpret_cast<const void*>(decode_attention_kernel<kModeFast>)
+                   : mode == kModeAdapter ? reinterpret_cast<const void*>(decode_attention_kernel<kModeAdapter>)
+                                          : reinterpret_cast<const void*>(decode_attention_kernel<kModeGeneral>);
   // Ring stages: as many as fit while a split-combine CTA still fits beside the page-pass CTA
   // on one SM (so it starts, and finishes the dense tail, while the page pass runs).
   const int ring_bytes = ring_budget(fn) - P.smem_stage_off;
@@ -1322,8 +1378,8 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
   if (P.n_stages < 2 * kConsumers)
     return fail(TP_ERR_UNSUPPORTED, "tp_decode_attention: not enough shared memory for the page ring");
   const int smem = P.smem_stage_off + P.n_stages * P.stage_bytes;
-  static int attr_bytes[2] = {0, 0};
-  int& have = attr_bytes[fast ? 1 : 0];
+  static int attr_bytes[3] = {0, 0, 0};
+  int& have = attr_bytes[mode];
   if (smem > have) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     // All of the unified L1/shared array as shared memory, so the split-combine CTAs fit beside
@@ -1351,8 +1407,9 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
     ma[0].val.programmaticStreamSerializationAllowed = 1;
     mc.attrs = ma;
     mc.numAttrs = 1;
-    const cudaError_t e = fast ? cudaLaunchKernelEx(&mc, decode_attention_kernel<true>, P)
-                               : cudaLaunchKernelEx(&mc, decode_attention_kernel<false>, P);
+    const cudaError_t e = mode == kModeFast      ? cudaLaunchKernelEx(&mc, decode_attention_kernel<kModeFast>, P)
+                          : mode == kModeAdapter ? cudaLaunchKernelEx(&mc, decode_attention_kernel<kModeAdapter>, P)
+                                                 : cudaLaunchKernelEx(&mc, decode_attention_kernel<kModeGeneral>, P);
     if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_decode_attention: ") + cudaGetErrorString(e));
   }
   // Split combine as a programmatic dependent launch of the attention grid.
