@@ -368,8 +368,9 @@ def run_gpu(args):
                        "l2": "inputs larger than L2 (2.48 GB of pages per step vs 126 MB L2)"},
             "decode_tokens_per_s": 1000.0 / ms_step,
             # Rank 0's kernels per layer: the page pass and the PDL split-combine of
-            # tp_decode_step (N=1) or tp_decode_attention, plus tp_combine_partials when sharded.
-            "gpu_launches": args.steps * LAYERS * (2 if world == 1 else 3),
+            # tp_decode_step (N=1) or tp_decode_attention_sharded (the cross-GPU merge runs
+            # inside the split combine).
+            "gpu_launches": args.steps * LAYERS * 2,
             "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary(),
             "device_errors": err,
         }

@@ -121,9 +121,11 @@ def exchange_attention(rt: TurboPolarKVCacheRuntime, q: torch.Tensor, exchange: 
 
 
 class ShardedDecodeStep:
-    """One captured decode step over all layers: local attention partial (the last rank appends
-    the new token in the same call, tp_decode_step), NCCL all-gather, combine.  The graph must
-    be released (``release()``) before the process group is destroyed."""
+    """One captured decode step over all layers (the last rank appends the new token in the same
+    call, tp_decode_step).  With ``exchange`` (the default) each layer is one sharded attention
+    call that merges the ranks' partials inside its launch over NVLink; otherwise a local
+    partial, an NCCL all-gather and tp_combine_partials.  The graph must be released
+    (``release()``) before the process group is destroyed."""
 
     def __init__(self, layers: List[TurboPolarKVCacheRuntime], k_in, v_in, q_in, out, rank: int, world: int,
                  group=None, exchange: bool = True):
