@@ -289,39 +289,52 @@ def run_gpu(args):
     value = step_bytes / args.steps / (ms_step * 1e-3) / 1e9
 
     # ---- roofline: attention kernel alone, per launch, on its own stream (graph of 32 launches).
-    kern_ms = None
-    roof = None
-    if world == 1 or True:
-        att_graph = torch.cuda.CUDAGraph()
+    def graph_us(launch_all, reps=20):
+        """Device time per launch of a captured graph of LAYERS attention calls."""
+        g = torch.cuda.CUDAGraph()
         torch.cuda.synchronize()
-        with torch.cuda.graph(att_graph):
-            for i in range(LAYERS):
-                graph.launch_attention(layers[i], q_in[i], out[i], cfg.attention_scale,
-                                       partial_out=step.partial_buffer(i) if world > 1 else None)
+        with torch.cuda.graph(g):
+            launch_all()
         for _ in range(3):
-            att_graph.replay()
+            g.replay()
         torch.cuda.synchronize()
-        reps = 20
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record()
         for _ in range(reps):
-            att_graph.replay()
+            g.replay()
         e2.record()
         torch.cuda.synchronize()
-        kern_ms = s2.elapsed_time(e2) / (reps * LAYERS)
-        rt0 = layers[0]
-        launch_bytes = attention_bytes(rt0.n_pages, rt0.tail_len, hq=HQ)
-        peak, peak_kind = _peaks()
-        achieved = launch_bytes / (kern_ms * 1e-3) / 1e9
-        tr = _traffic_from_profile()
-        traffic = None
-        if tr and world == 1:
-            traffic = int(tr["dram_bytes_per_launch"] * (launch_bytes / tr["algorithmic_bytes_per_launch"]))
-        roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs", "kernel": "decode_attention_kernel",
-                "launch_us": kern_ms * 1e3, "algorithmic_bytes_per_launch": launch_bytes,
-                "bytes_per_context_token": HKV * 296 // max(world, 1) if world == 1 else HKV * 296}
-        del att_graph
+        del g
+        return s2.elapsed_time(e2) / (reps * LAYERS) * 1e3
+
+    # One call per layer, each on its own cache with its own query and output (consecutive
+    # calls are independent, so a page pass may stream while the previous call finishes).
+    kern_us = graph_us(lambda: [graph.launch_attention(layers[i], q_in[i], out[i], cfg.attention_scale,
+                                                       partial_out=step.partial_buffer(i) if world > 1 else None)
+                                for i in range(LAYERS)])
+    # The same calls with each layer's query read from the previous layer's output, as in a
+    # model: every call then waits for the previous one to complete before its page pass
+    # streams, so this is the latency of one dependent call.
+    dep_us = None
+    if world == 1:
+        dep_out = torch.empty((LAYERS, 1, HQ, D), dtype=torch.float16, device=dev)
+        dep_us = graph_us(lambda: [graph.launch_attention(layers[i], q_in[0] if i == 0 else dep_out[i - 1],
+                                                          dep_out[i], cfg.attention_scale) for i in range(LAYERS)])
+    rt0 = layers[0]
+    launch_bytes = attention_bytes(rt0.n_pages, rt0.tail_len, hq=HQ)
+    peak, peak_kind = _peaks()
+    achieved = launch_bytes / (kern_us * 1e-6) / 1e9
+    tr = _traffic_from_profile()
+    traffic = None
+    if tr and world == 1:
+        traffic = int(tr["dram_bytes_per_launch"] * (launch_bytes / tr["algorithmic_bytes_per_launch"]))
+    roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs", "kernel": "decode_attention_kernel",
+            "launch_us": kern_us, "algorithmic_bytes_per_launch": launch_bytes,
+            "bytes_per_context_token": HKV * 296}
+    if dep_us is not None:
+        roof["dependent_launch_us"] = dep_us
+        roof["dependent_frac"] = launch_bytes / (dep_us * 1e-6) / 1e9 / peak
 
     # ---- e2e: host inputs -> device, graph step, outputs -> host, every step.
     h_in = d_in.cpu().pin_memory()

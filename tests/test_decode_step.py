@@ -131,6 +131,46 @@ def test_decode_step_graph_replay_matches_eager():
     assert torch.equal(g_rt.d_state[:5], e_rt.d_state[:5])
 
 
+@pytest.mark.parametrize("chained", [False, True])
+def test_layers_back_to_back_match_one_at_a_time(chained):
+    """Decode steps of several caches launched back to back, nothing else between them in the
+    stream: a layer's page pass may then stream while the previous layer's kernels finish, which
+    must change no result (bit for bit against the same steps run one at a time, flushes
+    included).  With ``chained`` every layer's query is the previous layer's output, a
+    dependency the library has to see and wait for."""
+    from turbopolar_b200 import TurboPolarConfig, TurboPolarKVCacheRuntime
+    cfg = TurboPolarConfig(num_q_heads=32, num_kv_heads=8)
+    n_layers, prefill, steps = 4, 64 * 40 + 60, 8  # each cache completes a page on step 3
+    kv = [kv_inputs(41 + i, 8, prefill + steps, np.float16) for i in range(n_layers)]
+    q = T(np.random.default_rng(40).standard_normal((steps, n_layers, 1, 32, 128)).astype(np.float16))
+    kin = [[T(kv[i][0][:, :, t:t + 1]) for t in range(prefill, prefill + steps)] for i in range(n_layers)]
+    vin = [[T(kv[i][1][:, :, t:t + 1]) for t in range(prefill, prefill + steps)] for i in range(n_layers)]
+    runs = []
+    for serial in (False, True):
+        rts = [TurboPolarKVCacheRuntime(cfg, max_seq_len=prefill + steps) for _ in range(n_layers)]
+        for i, rt in enumerate(rts):
+            rt.append(T(kv[i][0][:, :, :prefill]), T(kv[i][1][:, :, :prefill]))
+        out = torch.empty((steps, n_layers, 1, 32, 128), dtype=torch.float16, device=DEV)
+        torch.cuda.synchronize()
+        for t in range(steps):
+            for i, rt in enumerate(rts):
+                qi = out[t, i - 1] if chained and i > 0 else q[t, i]
+                rt.decode_step(kin[i][t], vin[i][t], qi, out=out[t, i])
+                if serial:
+                    torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        runs.append((out, rts))
+    (a, ra), (b, rb) = runs
+    assert torch.equal(a, b)
+    for x, y in zip(ra, rb):
+        assert torch.equal(x.d_state[:5], y.d_state[:5])
+        assert x.read_device_error() == 0
+    last = prefill + steps
+    want = oracle_attention(q[steps - 1, 0, 0].cpu().numpy(), kv[0][0][:, :, :last], kv[0][1][:, :, :last],
+                            fmt_of(cfg), False, cfg.attention_scale)
+    assert np.max(np.abs(a[steps - 1, 0, 0].float().cpu().numpy() - want)) < ATOL
+
+
 def test_decode_step_c_abi_errors():
     from turbopolar_b200 import _lib
     lib = _lib.lib()

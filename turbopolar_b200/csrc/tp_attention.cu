@@ -34,6 +34,7 @@
 #include <cstring>
 #include <cmath>
 #include <mutex>
+#include <unordered_map>
 
 #include "tp_codec.cuh"
 
@@ -75,6 +76,9 @@ struct AttnParams {
   int q_f32;
   int num_q_heads, num_kv_heads, group, nqc, gmax;
   int main_grid;  // CTAs of the page pass
+  // The previous call launched on this stream writes nothing this call reads: the page pass
+  // streams before griddepcontrol.wait (the host decides; see independent_of_previous).
+  int spec;
   // Fused decode step: one new token per KV head (k_new/v_new, tail dtype, heads
   // new_head_stride elements apart) appended before attention; wpool is the writable pool.
   int fused;
@@ -561,21 +565,31 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   auto produce_range = [&](int j0, int j1) {
     for (int j = j0; j < j1 && pcons + kConsumers * j < pt.n && !timed_out; ++j) produce(pcons, j);
   };
-  // Each consumer's first S units go in flight now, on the partition of the page count read
-  // now.  Every page below the newest one was written by a launch that had completed before
-  // the previous kernel in the stream started, so copies of those are valid whatever that
-  // kernel does; the newest page may be the one it is writing (an append that completed a
-  // page), so nothing is issued early if the first units touch it.
-  bool early = pt.active;
-  for (int k = 0; early && k < min(R, pt.n); ++k) early = unit_ref(pt, k).y < pt.n_pages - 1;
-  if (early && issuer) produce_range(0, S);
+  bool early = false;
+  tp_state st = s_pre;
+  if (P.spec) {
+    // The previous kernel in the stream writes nothing this launch reads (the host compared
+    // the two calls' buffers), so the state read above is final and the whole pass runs
+    // now; the wait comes before the partials are written (the workspace may be shared with
+    // the previous call, whose split combine reads its own partials until it completes).  The
+    // split-combine grid may become resident at once.
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  } else {
+    // Each consumer's first S units go in flight now, on the partition of the page count read
+    // now.  Every page below the newest one was written by a launch that had completed before
+    // the previous kernel in the stream started, so copies of those are valid whatever that
+    // kernel does; the newest page may be the one it is writing (an append that completed a
+    // page), so nothing is issued early if the first units touch it.
+    early = pt.active;
+    for (int k = 0; early && k < min(R, pt.n); ++k) early = unit_ref(pt, k).y < pt.n_pages - 1;
+    if (early && issuer) produce_range(0, S);
 
-  asm volatile("griddepcontrol.wait;\n" ::: "memory");
-  // Let the split-combine grid become resident now; it waits for this grid to complete.
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-
-  const tp_state st = read_state(P);
-  if (min(max(st.n_pages, 0), P.page_capacity) != pt.n_pages) {
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    // Let the split-combine grid become resident now; it waits for this grid to complete.
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+    st = read_state(P);
+  }
+  if (!P.spec && min(max(st.n_pages, 0), P.page_capacity) != pt.n_pages) {
     // The previous kernel appended to this cache: let the early copies land, reset the
     // barriers and start again on the new partition.
     if (early && issuer) {
@@ -661,6 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
       else store_empty_partial(rec1, gmax, lane);
     }
   }
+  if (P.spec) asm volatile("griddepcontrol.wait;\n" ::: "memory");
   __syncthreads();
 
   // Merge the warps of each segment and publish this CTA's partial; the split-combine kernel
@@ -1246,6 +1261,43 @@ static int grid_size(int num_kv_heads, int num_q_heads) {
   return max(num_sms(), num_kv_heads * nqc);
 }
 
+// Device byte ranges [lo, hi) that one call reads or writes.
+struct Span {
+  uintptr_t lo, hi;
+};
+constexpr int kMaxSpans = 8;
+struct Spans {
+  Span s[kMaxSpans];
+  int n = 0;
+  void add(const void* p, size_t bytes) {
+    if (p && bytes && n < kMaxSpans) s[n++] = Span{uintptr_t(p), uintptr_t(p) + bytes};
+  }
+  bool meets(const Spans& o) const {
+    for (int i = 0; i < n; ++i)
+      for (int j = 0; j < o.n; ++j)
+        if (s[i].lo < o.s[j].hi && o.s[j].lo < s[i].hi) return true;
+    return false;
+  }
+};
+
+static std::mutex g_stream_mutex;
+static std::unordered_map<cudaStream_t, Spans> g_last_writes;
+
+// Whether a call may stream its pages before the previous call launched on the same stream
+// has completed, and records this call's writes as the stream's last.  Only this library's
+// kernels let a dependent grid start before they complete (griddepcontrol.launch_dependents),
+// and any other kernel launched between two calls starts after the first call has completed,
+// so the one call to compare with is the previous one of this library on the stream: the
+// answer is yes when nothing it writes is read by this call.  The workspace is left out of
+// both sides: the page pass writes its partials only after griddepcontrol.wait.
+static bool independent_of_previous(cudaStream_t s, const Spans& reads, const Spans& writes, bool allow) {
+  std::lock_guard<std::mutex> lock(g_stream_mutex);
+  const auto it = g_last_writes.find(s);
+  const bool ok = allow && (it == g_last_writes.end() || !it->second.meets(reads));
+  g_last_writes[s] = writes;
+  return ok;
+}
+
 }  // namespace tp
 
 using namespace tp;
@@ -1393,9 +1445,36 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
                                    " bytes of shared memory: " + cudaGetErrorString(e));
     have = smem;
   }
+  {
+    const size_t pool_bytes = size_t(hkv) * pool->page_capacity;
+    const size_t tail_bytes = size_t(hkv) * kPage * kD * (P.tail_f32 ? 4 : 2);
+    Spans reads, writes;
+    reads.add(q, size_t(num_q_heads) * kD * (P.q_f32 ? 4 : 2));
+    reads.add(pool->pages, pool_bytes * L.page_bytes);
+    reads.add(pool->radii_scales, pool_bytes * sizeof(__half));
+    reads.add(tail->k, tail_bytes);
+    reads.add(tail->v, tail_bytes);
+    reads.add(d_state, TP_STATE_WORDS * sizeof(int32_t));
+    if (out) writes.add(out, size_t(num_q_heads) * kD * sizeof(__half));
+    else writes.add(partial_out, size_t(num_q_heads) * TP_PARTIAL_FLOATS * sizeof(float));
+    if (step) {
+      const size_t new_bytes = (size_t(hkv - 1) * step->head_stride + kD) * (P.tail_f32 ? 4 : 2);
+      reads.add(step->k_new, new_bytes);
+      reads.add(step->v_new, new_bytes);
+      writes.add(d_state, TP_STATE_WORDS * sizeof(int32_t));
+      writes.add(tail->k, tail_bytes);
+      writes.add(tail->v, tail_bytes);
+      writes.add(pool->pages, pool_bytes * L.page_bytes);
+      writes.add(pool->radii_scales, pool_bytes * sizeof(__half));
+    }
+    // A sharded call's split combine exchanges records with the other ranks under an epoch
+    // that every call on the buffer advances, so it never overlaps its predecessor.
+    P.spec = independent_of_previous(s, reads, writes, P.xworld == 0) ? 1 : 0;
+  }
   // The page pass is a programmatic dependent of whatever precedes it in the stream (a no-op
   // unless that kernel triggers early, as the split combine of a previous call does): its
-  // CTAs load their code tables while that kernel finishes.
+  // CTAs load their code tables while that kernel finishes, or, when the previous call is
+  // independent of this one, run the whole pass.
   {
     cudaLaunchConfig_t mc = {};
     mc.gridDim = dim3(grid);
