@@ -4,16 +4,16 @@
 // (rfsn_v11/kernels/turbo_polar/tqpolar_online_attention.metal:197-629) with the numerics of
 // the bridge's CPU fallback (rfsn_v11/kernels/turbo_polar/metal.py:293-332) as the target.
 //
-// Work decomposition.  A "unit" is one half page (32 tokens) of one (KV head, query chunk), or
-// that head's dense tail.  The units of all heads form one flat list cut into gridDim.x
-// contiguous ranges, one per CTA, so every SM streams the same number of pages whatever the
-// head count or context length; a range spans at most two heads ("segments").  Each of the 8
-// warps of a CTA takes a contiguous slice of each segment and streams exactly the rows it
-// consumes through a private double buffer in shared memory (cp.async, 16 bytes per lane; rows
-// of radii and value codes XOR-swizzled so the fragment loads below are bank-conflict free),
-// so warps never wait on one another inside the loop.
+// Work decomposition.  A "unit" is one half page (32 tokens) of one (KV head, query chunk of
+// at most 8 heads): one contiguous block of the page pool.  The units of all heads form one flat
+// list cut into gridDim.x contiguous ranges, one per CTA (one CTA per SM), so every SM streams
+// the same number of bytes whatever the head count or context length; a range spans at most
+// two heads ("segments").  Inside a CTA, 7 compute warps take units w, w+7, ... of the range
+// and one copy warp streams them: lane w issues one cp.async.bulk per unit of compute warp w
+// into that warp's own ring stages (full/empty mbarriers per stage), so no wait ever runs
+// ahead of its barrier's phase and compute warps never wait on one another.
 //
-// Per half page a warp computes, with mma.sync m16n8k16 (fp16 in, fp32 accumulate):
+// Per half page a compute warp computes, with mma.sync m16n8k16 (fp16 in, fp32 accumulate):
 //   S^T[token][head] = K[token][dim] . Q^T[dim][head]      M = 16 tokens, N = 8 query heads
 // where every lane decodes exactly the key pairs its A fragment holds: lane (g, t) owns pairs
 // [16t, 16t+16) of tokens g and g+8, each pair k = radius * (cos, sin)(code) from a 16-entry
@@ -26,10 +26,12 @@
 // + byte, byte = code ^ 0x80).  The bias is removed at the end with a ones-row tile per group
 // that accumulates sum_t P*scale_g alongside (O = O' - 1152 * sum).
 //
-// Split combine.  Warps of a CTA merge through shared memory; CTAs that share a head write a
-// partial (m, l, o[128]) to the workspace and the last to arrive (atomic ticket per head)
-// merges them in parallel and writes the fp16 output, then resets the ticket, all in the same
-// launch.
+// Split combine.  The warps of a CTA merge through shared memory and the CTA writes one
+// partial (m, l, o[128]) per query head and segment to the workspace.  A second kernel, launched
+// as a programmatic dependent of the page pass, computes the dense-tail partial (and, in a
+// decode step, appends the new token) while the page pass runs, then waits for it to complete
+// and merges the partials of each query head into the fp16 output (sharded: with the other
+// ranks' records, exchanged over NVLink in the same launch).
 #include <cfloat>
 #include <cstring>
 #include <cmath>

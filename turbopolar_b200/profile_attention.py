@@ -5,7 +5,9 @@
 Builds enough independent layers that their pages exceed 4x the 126 MB L2 (so every launch
 reads cold data), captures one launch per layer in a CUDA graph and replays it; the per-launch
 device time comes from CUDA events around the replays on the launching stream.  Prints the
-time and the achieved GB/s of algorithmic bytes (compressed pages + dense tail + q + out).
+time and the achieved GB/s of algorithmic bytes (compressed pages + dense tail + q + out), for
+independent launches (every layer reads the same query) and for a dependent chain (each
+layer's query is the previous layer's output).
 ``--launches N`` instead issues N plain launches over the layers (for ncu: one kernel per
 launch, no graph).
 """
@@ -74,22 +76,32 @@ def main(argv=None):
         torch.cuda.synchronize()
         print(json.dumps({"plain_launches": a.launches}))
         return
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        for rt, o in zip(layers, outs):
-            rt.attention(q, out=o)
-    for _ in range(3):
-        g.replay()
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(a.reps):
-        g.replay()
-    e.record()
-    torch.cuda.synchronize()
-    us = s.elapsed_time(e) * 1e3 / (a.reps * len(layers))
+
+    def per_launch_us(chain: bool) -> float:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i, (rt, o) in enumerate(zip(layers, outs)):
+                rt.attention(outs[i - 1] if chain and i > 0 else q, out=o)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(a.reps):
+            g.replay()
+        e.record()
+        torch.cuda.synchronize()
+        del g
+        return s.elapsed_time(e) * 1e3 / (a.reps * len(layers))
+
+    # Independent calls (each layer reads the same query), then a dependent chain (each layer's
+    # query is the previous layer's output, so no call may start streaming before the previous
+    # one has completed).
+    us = per_launch_us(False)
+    dep = per_launch_us(True)
     print(json.dumps({"ctx": a.ctx, "hq": a.hq, "hkv": a.hkv, "format": a.format, "layers": len(layers),
-                      "us_per_launch": us, "bytes_per_launch": nbytes, "gbs": nbytes / us / 1e3}))
+                      "us_per_launch": us, "bytes_per_launch": nbytes, "gbs": nbytes / us / 1e3,
+                      "us_per_launch_dependent": dep, "gbs_dependent": nbytes / dep / 1e3}))
 
 
 if __name__ == "__main__":
