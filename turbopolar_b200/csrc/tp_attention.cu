@@ -507,6 +507,7 @@ template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __grid_constant__ AttnParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ tp_state s_pre;  // cache state as read before the wait, one read for the CTA
+  __shared__ float s_wt[2][kMaxHeads][kConsumers + 1];  // merge weights, then the maximum
   uint32_t* lut = reinterpret_cast<uint32_t*>(smem + P.smem_lut_off);
   float* merge = reinterpret_cast<float*>(smem + P.smem_merge_off);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.smem_bar_off);
@@ -541,8 +542,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
     fence_mbar_init();
   };
   if (tid == 0) {
+    const tp_state st0 = read_state(P);  // loads in flight while the barriers are set up
     init_barriers();
-    s_pre = read_state(P);
+    s_pre = st0;
   }
   __syncthreads();  // barriers initialised and the state read before any producer issues
   Part pt = make_part(P, s_pre, c);
@@ -681,33 +683,43 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   __syncthreads();
 
   // Merge the warps of each segment and publish this CTA's partial; the split-combine kernel
-  // (launched as a programmatic dependent of this grid) merges the CTAs of every head.
+  // (launched as a programmatic dependent of this grid) merges the CTAs of every head.  The
+  // weight of warp w's partial for head h, exp2(m_w - M_h), is computed once per (segment,
+  // head, warp) and read by every channel.
+  auto seg_recs = [&](int s) { return s == 0 ? merge : reinterpret_cast<const float*>(ring); };
+  auto seg_stride = [&](int s) { return s == 0 ? rec_stride : P.stage_bytes / int(sizeof(float)); };
+  for (int i = tid; i < nseg * gmax * kConsumers; i += kThreads) {
+    const int s = i / (gmax * kConsumers), h = (i / kConsumers) % gmax, w = i % kConsumers;
+    const float* recs = seg_recs(s) + h * TP_PARTIAL_FLOATS;
+    const int wstride = seg_stride(s);
+    float M = recs[0];
+#pragma unroll
+    for (int v = 1; v < kConsumers; ++v) M = fmaxf(M, recs[v * wstride]);
+    const float m = recs[w * wstride];
+    s_wt[s][h][w] = (m == -INFINITY) ? 0.f : exp2_approx(m - M);
+    if (w == 0) s_wt[s][h][kConsumers] = M;
+  }
+  __syncthreads();
   for (int s = 0; s < nseg; ++s) {
     const int vh = vh_first + s;
     const int chunk = vh % P.nqc;
     const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
     float* slot = P.ws_partials + int64_t(c * 2 + s) * kPartialStride;
-    const float* recs = s == 0 ? merge : reinterpret_cast<const float*>(ring);
-    const int wstride = s == 0 ? rec_stride : P.stage_bytes / int(sizeof(float));
+    const float* recs = seg_recs(s);
+    const int wstride = seg_stride(s);
 #pragma unroll 1
     for (int i = tid; i < gc * kD; i += kThreads) {
       const int h = i >> 7, d = i & (kD - 1);
-      float m[kConsumers];
-#pragma unroll
-      for (int w = 0; w < kConsumers; ++w) m[w] = recs[w * wstride + h * TP_PARTIAL_FLOATS];
-      float M = m[0];
-#pragma unroll
-      for (int w = 1; w < kConsumers; ++w) M = fmaxf(M, m[w]);
       float L = 0.f, O = 0.f;
 #pragma unroll
       for (int w = 0; w < kConsumers; ++w) {
         const float* r = recs + w * wstride + h * TP_PARTIAL_FLOATS;
-        const float f = (m[w] == -INFINITY) ? 0.f : exp2_approx(m[w] - M);
+        const float f = s_wt[s][h][w];
         L = fmaf(r[1], f, L);
         O = fmaf(r[2 + d], f, O);
       }
       float* out = slot + h * kRecFloats;
-      if (d == 0) { out[0] = M; out[1] = L; }
+      if (d == 0) { out[0] = s_wt[s][h][kConsumers]; out[1] = L; }
       out[2 + d] = O;
     }
   }
