@@ -162,7 +162,10 @@ size_t tp_decode_attention_workspace_size(int32_t num_kv_heads, int32_t num_q_he
  * float16 as the reference's kernels read them).  With partial_out non-NULL the kernel
  * writes, instead of `out`, one unnormalised partial per query head
  * [H_q][TP_PARTIAL_FLOATS] = (m in log2 units, l, o[128]) for a cross-shard log-sum-exp
- * merge (tp_combine_partials).  `state` is used when d_state is NULL. */
+ * merge (tp_combine_partials).  `state` is used when d_state is NULL.  When the previous call
+ * of this library on `stream` writes no buffer this call reads (another cache and another
+ * query), this call's page pass starts streaming before that call's kernels have completed;
+ * the library compares the buffers' addresses itself. */
 int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state state,
                         const int32_t* d_state, const void* q, int32_t q_dtype,
                         int32_t num_q_heads, float scale, void* out, float* partial_out,

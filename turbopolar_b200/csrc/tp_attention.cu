@@ -1036,8 +1036,9 @@ __global__ void __launch_bounds__(kCombineThreads, 4) split_combine_kernel(const
   const int vh = blockIdx.x / P.gmax, h = blockIdx.x % P.gmax;
   const int kvh = vh / P.nqc, chunk = vh % P.nqc;
   const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
-  // The next page pass in the stream may start its prologue now; it waits for this grid to
-  // complete before it reads anything.
+  // The next page pass in the stream may start now: it waits for this grid to complete before
+  // it reads anything this call writes (or, when it shares no buffer with this call, before it
+  // writes its partials).
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
   // One thread reads the state words; with the fused step it then takes a ticket, and the
