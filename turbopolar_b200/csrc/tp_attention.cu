@@ -1280,14 +1280,18 @@ static int grid_size(int num_kv_heads, int num_q_heads) {
 struct Span {
   uintptr_t lo, hi;
 };
-constexpr int kMaxSpans = 8;
+constexpr int kMaxSpans = 12;
 struct Spans {
   Span s[kMaxSpans];
   int n = 0;
+  bool all = false;  // more ranges than fit: treated as overlapping everything
   void add(const void* p, size_t bytes) {
-    if (p && bytes && n < kMaxSpans) s[n++] = Span{uintptr_t(p), uintptr_t(p) + bytes};
+    if (!p || !bytes) return;
+    if (n < kMaxSpans) s[n++] = Span{uintptr_t(p), uintptr_t(p) + bytes};
+    else all = true;
   }
   bool meets(const Spans& o) const {
+    if (all || o.all) return true;
     for (int i = 0; i < n; ++i)
       for (int j = 0; j < o.n; ++j)
         if (s[i].lo < o.s[j].hi && o.s[j].lo < s[i].hi) return true;
@@ -1482,9 +1486,16 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
       writes.add(pool->pages, pool_bytes * L.page_bytes);
       writes.add(pool->radii_scales, pool_bytes * sizeof(__half));
     }
-    // A sharded call's split combine exchanges records with the other ranks under an epoch
-    // that every call on the buffer advances, so it never overlaps its predecessor.
-    P.spec = independent_of_previous(s, reads, writes, P.xworld == 0) ? 1 : 0;
+    // A sharded call's split combine reads and advances the epoch in this rank's exchange
+    // buffer before its wait, so two calls on one exchange never overlap; calls on different
+    // exchanges (one per layer) may.  The other ranks' buffers are written only after the
+    // wait.
+    if (x) {
+      const size_t xb = x_epoch_off(P.xworld, num_q_heads) + 256;
+      reads.add(P.xbuf[P.xrank], xb);
+      writes.add(P.xbuf[P.xrank], xb);
+    }
+    P.spec = independent_of_previous(s, reads, writes, true) ? 1 : 0;
   }
   // The page pass is a programmatic dependent of whatever precedes it in the stream (a no-op
   // unless that kernel triggers early, as the split combine of a previous call does): its
