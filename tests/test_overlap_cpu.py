@@ -1,0 +1,133 @@
+"""When may a decode-attention call overlap the previous call on its stream (CPU).
+
+The page pass of a call streams before its grid-dependency wait only when the previous call of
+the library on the same stream writes nothing the call reads (tp_overlap.h: ``call_spans`` and
+``StreamLog``).  A wrong "independent" would let a page pass read a cache, a query or an
+exchange epoch that the previous call is still writing, so the decision is checked here case by
+case: a small C++ driver is compiled with g++ against the header and run.
+"""
+
+import os
+import shutil
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CSRC = os.path.join(ROOT, "turbopolar_b200", "csrc")
+
+DRIVER = r"""
+#include <cstdio>
+#include <cstdlib>
+#include "tp_overlap.h"
+using namespace tp;
+
+static unsigned char mem[1 << 20];
+static const void* at(size_t off) { return mem + off; }
+
+// One cache (pool, scales, tail, state) at `base`, a query and an output.
+static CallBuffers call(size_t base, size_t q, size_t out, bool step) {
+  CallBuffers b;
+  b.q = at(q); b.q_bytes = 8192;
+  b.pages = at(base); b.pages_bytes = 40000;
+  b.radii_scales = at(base + 40000); b.radii_scales_bytes = 512;
+  b.tail_k = at(base + 41000); b.tail_v = at(base + 50000); b.tail_bytes = 8192;
+  b.d_state = at(base + 60000); b.state_bytes = 24;
+  b.out = at(out); b.out_bytes = 8192;
+  if (step) { b.step = true; b.k_new = at(q + 9000); b.v_new = at(q + 10000); b.new_bytes = 256; }
+  return b;
+}
+
+static bool run(StreamLog& log, const void* stream, const CallBuffers& b) {
+  Spans r, w;
+  call_spans(b, r, w);
+  return log.independent(stream, r, w);
+}
+
+#define CHECK(cond) do { if (!(cond)) { std::printf("FAIL line %d: %s\n", __LINE__, #cond); std::exit(1); } } while (0)
+
+int main() {
+  const void* s1 = &mem[0];
+  const void* s2 = &mem[1];
+  {  // the first call on a stream; then layers of a decode step (other caches, queries, outputs)
+    StreamLog log;
+    CHECK(run(log, s1, call(0, 300000, 400000, true)));
+    CHECK(run(log, s1, call(100000, 310000, 410000, true)));
+    CHECK(run(log, s1, call(200000, 320000, 420000, true)));
+  }
+  {  // two decode steps on one cache: the second reads the state, tail and pool the first writes
+    StreamLog log;
+    run(log, s1, call(0, 300000, 400000, true));
+    CHECK(!run(log, s1, call(0, 310000, 410000, true)));
+  }
+  {  // a decode step, then plain attention on the same cache: it reads what the step wrote
+    StreamLog log;
+    run(log, s1, call(0, 300000, 400000, true));
+    CHECK(!run(log, s1, call(0, 310000, 410000, false)));
+  }
+  {  // plain attention twice on one cache writes only the outputs: independent
+    StreamLog log;
+    run(log, s1, call(0, 300000, 400000, false));
+    CHECK(run(log, s1, call(0, 310000, 410000, false)));
+  }
+  {  // the query is the previous call's output, whole or in part
+    StreamLog log;
+    run(log, s1, call(0, 300000, 400000, false));
+    CHECK(!run(log, s1, call(100000, 400000, 410000, false)));
+    run(log, s1, call(0, 300000, 420000, false));
+    CHECK(!run(log, s1, call(100000, 420000 + 8191, 430000, false)));
+    run(log, s1, call(0, 300000, 440000, false));
+    CHECK(run(log, s1, call(100000, 440000 + 8192, 460000, false)));  // adjacent, not overlapping
+  }
+  {  // the new token of a step is the previous call's output
+    StreamLog log;
+    run(log, s1, call(0, 300000, 409000, false));
+    CHECK(!run(log, s1, call(100000, 400000, 430000, true)));  // k_new at 409000
+  }
+  {  // the previous call's output lands in this call's tail or state words
+    StreamLog log;
+    run(log, s1, call(0, 300000, 100000 + 41000, false));
+    CHECK(!run(log, s1, call(100000, 310000, 450000, false)));
+    run(log, s1, call(0, 300000, 100000 + 60000 - 100, false));
+    CHECK(!run(log, s1, call(100000, 320000, 460000, false)));
+  }
+  {  // streams are logged separately
+    StreamLog log;
+    run(log, s1, call(0, 300000, 400000, true));
+    CHECK(run(log, s2, call(0, 310000, 410000, true)));
+    CHECK(!run(log, s1, call(0, 320000, 420000, true)));
+  }
+  {  // sharded calls: one exchange per layer overlaps, a shared exchange does not
+    StreamLog log;
+    CallBuffers a = call(0, 300000, 400000, true), b = call(100000, 310000, 410000, true);
+    a.exchange = at(600000); a.exchange_bytes = 70000;
+    b.exchange = at(700000); b.exchange_bytes = 70000;
+    run(log, s1, a);
+    CHECK(run(log, s1, b));
+    CallBuffers c = call(200000, 320000, 420000, true);
+    c.exchange = at(700000); c.exchange_bytes = 70000;
+    CHECK(!run(log, s1, c));
+  }
+  {  // more ranges than fit count as overlapping everything
+    Spans r, w;
+    for (int i = 0; i < kMaxSpans + 1; ++i) r.add(at(1000 * i), 10);
+    w.add(at(900000), 10);
+    CHECK(r.all && r.meets(w) && w.meets(r));
+    Spans e;
+    CHECK(!e.meets(w));
+  }
+  std::printf("ok\n");
+  return 0;
+}
+"""
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
+def test_overlap_decisions(tmp_path):
+    src = tmp_path / "overlap_driver.cpp"
+    src.write_text(DRIVER)
+    exe = tmp_path / "overlap_driver"
+    subprocess.run(["g++", "-std=c++17", "-O1", "-I", CSRC, str(src), "-o", str(exe)], check=True,
+                   capture_output=True, timeout=120)
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert res.returncode == 0 and res.stdout.strip() == "ok", res.stdout + res.stderr

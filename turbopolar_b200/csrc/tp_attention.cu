@@ -36,9 +36,9 @@
 #include <cstring>
 #include <cmath>
 #include <mutex>
-#include <unordered_map>
 
 #include "tp_codec.cuh"
+#include "tp_overlap.h"
 
 namespace tp {
 
@@ -79,7 +79,7 @@ struct AttnParams {
   int num_q_heads, num_kv_heads, group, nqc, gmax;
   int main_grid;  // CTAs of the page pass
   // The previous call launched on this stream writes nothing this call reads: the page pass
-  // streams before griddepcontrol.wait (the host decides; see independent_of_previous).
+  // streams before griddepcontrol.wait (the host decides: StreamLog in tp_overlap.h).
   int spec;
   // Fused decode step: one new token per KV head (k_new/v_new, tail dtype, heads
   // new_head_stride elements apart) appended before attention; wpool is the writable pool.
@@ -1276,46 +1276,7 @@ static int grid_size(int num_kv_heads, int num_q_heads) {
   return max(num_sms(), num_kv_heads * nqc);
 }
 
-// Device byte ranges [lo, hi) that one call reads or writes.
-struct Span {
-  uintptr_t lo, hi;
-};
-constexpr int kMaxSpans = 12;
-struct Spans {
-  Span s[kMaxSpans];
-  int n = 0;
-  bool all = false;  // more ranges than fit: treated as overlapping everything
-  void add(const void* p, size_t bytes) {
-    if (!p || !bytes) return;
-    if (n < kMaxSpans) s[n++] = Span{uintptr_t(p), uintptr_t(p) + bytes};
-    else all = true;
-  }
-  bool meets(const Spans& o) const {
-    if (all || o.all) return true;
-    for (int i = 0; i < n; ++i)
-      for (int j = 0; j < o.n; ++j)
-        if (s[i].lo < o.s[j].hi && o.s[j].lo < s[i].hi) return true;
-    return false;
-  }
-};
-
-static std::mutex g_stream_mutex;
-static std::unordered_map<cudaStream_t, Spans> g_last_writes;
-
-// Whether a call may stream its pages before the previous call launched on the same stream
-// has completed, and records this call's writes as the stream's last.  Only this library's
-// kernels let a dependent grid start before they complete (griddepcontrol.launch_dependents),
-// and any other kernel launched between two calls starts after the first call has completed,
-// so the one call to compare with is the previous one of this library on the stream: the
-// answer is yes when nothing it writes is read by this call.  The workspace is left out of
-// both sides: the page pass writes its partials only after griddepcontrol.wait.
-static bool independent_of_previous(cudaStream_t s, const Spans& reads, const Spans& writes, bool allow) {
-  std::lock_guard<std::mutex> lock(g_stream_mutex);
-  const auto it = g_last_writes.find(s);
-  const bool ok = allow && (it == g_last_writes.end() || !it->second.meets(reads));
-  g_last_writes[s] = writes;
-  return ok;
-}
+static StreamLog g_stream_log;  // last call's writes per stream (tp_overlap.h)
 
 }  // namespace tp
 
@@ -1465,37 +1426,36 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
     have = smem;
   }
   {
-    const size_t pool_bytes = size_t(hkv) * pool->page_capacity;
-    const size_t tail_bytes = size_t(hkv) * kPage * kD * (P.tail_f32 ? 4 : 2);
-    Spans reads, writes;
-    reads.add(q, size_t(num_q_heads) * kD * (P.q_f32 ? 4 : 2));
-    reads.add(pool->pages, pool_bytes * L.page_bytes);
-    reads.add(pool->radii_scales, pool_bytes * sizeof(__half));
-    reads.add(tail->k, tail_bytes);
-    reads.add(tail->v, tail_bytes);
-    reads.add(d_state, TP_STATE_WORDS * sizeof(int32_t));
-    if (out) writes.add(out, size_t(num_q_heads) * kD * sizeof(__half));
-    else writes.add(partial_out, size_t(num_q_heads) * TP_PARTIAL_FLOATS * sizeof(float));
+    CallBuffers b;
+    const size_t pool_pages = size_t(hkv) * pool->page_capacity;
+    b.q = q;
+    b.q_bytes = size_t(num_q_heads) * kD * (P.q_f32 ? 4 : 2);
+    b.pages = pool->pages;
+    b.pages_bytes = pool_pages * L.page_bytes;
+    b.radii_scales = pool->radii_scales;
+    b.radii_scales_bytes = pool_pages * sizeof(__half);
+    b.tail_k = tail->k;
+    b.tail_v = tail->v;
+    b.tail_bytes = size_t(hkv) * kPage * kD * (P.tail_f32 ? 4 : 2);
+    b.d_state = d_state;
+    b.state_bytes = TP_STATE_WORDS * sizeof(int32_t);
+    // The kernels write partial_out when it is given, else out (write_result).
+    b.out = partial_out ? static_cast<void*>(partial_out) : out;
+    b.out_bytes = partial_out ? size_t(num_q_heads) * TP_PARTIAL_FLOATS * sizeof(float)
+                              : size_t(num_q_heads) * kD * sizeof(__half);
     if (step) {
-      const size_t new_bytes = (size_t(hkv - 1) * step->head_stride + kD) * (P.tail_f32 ? 4 : 2);
-      reads.add(step->k_new, new_bytes);
-      reads.add(step->v_new, new_bytes);
-      writes.add(d_state, TP_STATE_WORDS * sizeof(int32_t));
-      writes.add(tail->k, tail_bytes);
-      writes.add(tail->v, tail_bytes);
-      writes.add(pool->pages, pool_bytes * L.page_bytes);
-      writes.add(pool->radii_scales, pool_bytes * sizeof(__half));
+      b.step = true;
+      b.k_new = step->k_new;
+      b.v_new = step->v_new;
+      b.new_bytes = (size_t(hkv - 1) * step->head_stride + kD) * (P.tail_f32 ? 4 : 2);
     }
-    // A sharded call's split combine reads and advances the epoch in this rank's exchange
-    // buffer before its wait, so two calls on one exchange never overlap; calls on different
-    // exchanges (one per layer) may.  The other ranks' buffers are written only after the
-    // wait.
     if (x) {
-      const size_t xb = x_epoch_off(P.xworld, num_q_heads) + 256;
-      reads.add(P.xbuf[P.xrank], xb);
-      writes.add(P.xbuf[P.xrank], xb);
+      b.exchange = P.xbuf[P.xrank];
+      b.exchange_bytes = x_epoch_off(P.xworld, num_q_heads) + 256;
     }
-    P.spec = independent_of_previous(s, reads, writes, true) ? 1 : 0;
+    Spans reads, writes;
+    call_spans(b, reads, writes);
+    P.spec = g_stream_log.independent(s, reads, writes) ? 1 : 0;
   }
   // The page pass is a programmatic dependent of whatever precedes it in the stream (a no-op
   // unless that kernel triggers early, as the split combine of a previous call does): its
