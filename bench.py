@@ -14,7 +14,9 @@ Reported (one JSON line on rank 0):
   e2e       -- the same metric with every step's inputs copied from pinned host memory and the
                attention outputs copied back, inside the timed region
   roofline  -- the attention kernel alone, timed per launch with CUDA events, against the
-               measured HBM copy bandwidth
+               measured HBM copy bandwidth: 32 independent layers in a graph (consecutive
+               calls overlap), and as dependent_launch_us / dependent_frac the same launches
+               with each layer's query read from the previous layer's output (no overlap)
   cpu_baseline -- the NumPy oracle (the reference's CPU-fallback math) on a bounded sample
 
 Multi-GPU (torchrun, N>1): one sequence of N x 32K tokens per layer, split into contiguous
