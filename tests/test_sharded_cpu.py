@@ -4,7 +4,9 @@ Each rank holds a contiguous page range of every KV head (``sharded.page_range``
 rank also holds the dense tail), computes per-query-head partials (m, l, o), all-gathers them
 and merges with the log-sum-exp rule that ``tp_combine_partials`` implements; the merged
 output must equal single-device attention over the whole sequence.  The partials come from the
-oracle here (no GPU); the CUDA path runs the same protocol in ``test_sharded_gpu.py``.
+oracle here (no GPU); the CUDA path runs the same protocol in ``test_sharded_gpu.py``.  The
+rank-failure tests at the end run ``StepMonitor`` in three spawned processes over a TCP store,
+with the failures injected on the host.
 """
 
 import socket
@@ -91,3 +93,82 @@ def test_gloo_two_ranks_match_single_device():
     assert sorted(out.keys()) == [0, 1]
     for r in range(2):
         np.testing.assert_allclose(out[r], want, rtol=0, atol=1e-12)
+
+
+# ---------------------------------------------------------------------------- rank failures
+# StepMonitor (sharded.py) is the host-side check that every rank has reached a step before any
+# rank launches it.  Failures are injected on the host: a rank raises and leaves, exits, or skips
+# a step; the surviving ranks must raise RankFailure naming it, within the monitor's timeout,
+# before launching that step.
+STEPS = 5
+FAIL_AT = 3
+
+
+def _monitor_worker(rank, world, port, mode, out):
+    import os
+    import time
+    from datetime import timedelta
+    from turbopolar_b200.sharded import RankFailure, StepMonitor
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=timedelta(seconds=60))
+    mon = StepMonitor(rank, world, store=store, prefix="steps", timeout_s=2.0)
+    launched = []
+    t0 = time.monotonic()
+    try:
+        for k in range(1, STEPS + 1):
+            if rank == 1 and k == FAIL_AT and mode == "raise":
+                try:
+                    raise RuntimeError("injected failure")
+                except RuntimeError:
+                    out[rank] = ("left", launched, "")
+                    return
+            if rank == 1 and k == FAIL_AT and mode == "exit":
+                out[rank] = ("exited", launched, "")
+                os._exit(0)
+            if rank == 1 and k == FAIL_AT and mode == "skip":
+                continue
+            mon.step(k)
+            launched.append(k)  # stands for the step's launches
+            time.sleep(0.01)
+        out[rank] = ("ok", launched, "")
+    except RankFailure as e:
+        out[rank] = ("failure", launched, str(e), time.monotonic() - t0)
+    finally:
+        if rank == 0:
+            time.sleep(3.0)  # rank 0 serves the store; let the others finish their reads
+
+
+def _run_monitor(mode, world=3):
+    manager = mp.get_context("spawn").Manager()
+    out = manager.dict()
+    mp.start_processes(_monitor_worker, args=(world, _free_port(), mode, out), nprocs=world, join=True,
+                       start_method="spawn")
+    return dict(out)
+
+
+def test_step_monitor_all_ranks_healthy():
+    out = _run_monitor("none")
+    for r in range(3):
+        assert out[r][0] == "ok" and out[r][1] == list(range(1, STEPS + 1)), out[r]
+
+
+@pytest.mark.parametrize("mode", ["raise", "exit"])
+def test_step_monitor_detects_a_rank_that_left(mode):
+    out = _run_monitor(mode)
+    for r in (0, 2):
+        status, launched, msg, elapsed = out[r]
+        assert status == "failure", out[r]
+        assert launched == list(range(1, FAIL_AT)), out[r]  # nothing launched for the missing step
+        assert "rank 1 did not reach step 3" in msg
+        assert elapsed < 20.0
+
+
+def test_step_monitor_detects_a_skipped_step():
+    """A rank that skips a step is found at that step; the skipping rank, one step ahead, finds
+    that nobody else reached its next one."""
+    out = _run_monitor("skip")
+    for r in (0, 2):
+        status, launched, msg, _ = out[r]
+        assert status == "failure", out[r]
+        assert launched == list(range(1, FAIL_AT)) and "rank 1 did not reach step 3" in msg, out[r]
+    status, launched, msg, _ = out[1]
+    assert status == "failure" and launched == list(range(1, FAIL_AT)) and "did not reach step 4" in msg, out[1]

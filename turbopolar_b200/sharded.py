@@ -17,6 +17,7 @@ the NCCL path (``exchange=False``) writes ``partial_out``, all-gathers it and ru
 from __future__ import annotations
 
 import ctypes
+import time
 from typing import List, Tuple
 
 import torch
@@ -54,6 +55,56 @@ def sharded_attention(rt: TurboPolarKVCacheRuntime, q: torch.Tensor, group=None)
     dist.all_gather_into_tensor(gathered, part, group=group)
     out = torch.empty((B, Hq, 128), dtype=torch.float16, device=q.device)
     return combine(gathered, out)
+
+
+class RankFailure(RuntimeError):
+    """A rank did not reach a step of a sharded decode in time (it raised, exited or skipped)."""
+
+
+class StepMonitor:
+    """Host-side liveness of the ranks of a sharded decode.
+
+    Before launching step ``k`` every rank announces it in the process group's key-value store
+    (one key per rank and step) and waits, within ``timeout_s``, until every rank has announced
+    step ``k`` (``step``).  A rank that raised, exited or skipped the step never announces it,
+    so the others raise RankFailure on the host, naming it, instead of launching work that
+    would wait for its records (the peer exchange's bounded wait, or a collective).  Keys are
+    tested with ``store.check``, which never blocks; a rank deletes its own key of step k - 2
+    when it announces step k (every rank has passed step k - 1's check by then, so nobody reads
+    it any more).
+    """
+
+    def __init__(self, rank: int, world: int, store=None, prefix: str = "tp_steps", timeout_s: float = 30.0,
+                 poll_s: float = 0.001):
+        if store is None:
+            store = dist.distributed_c10d._get_default_store()
+        self.store, self.rank, self.world = store, rank, world
+        self.prefix, self.timeout_s, self.poll_s = prefix, float(timeout_s), float(poll_s)
+        self.steps = 0
+        self._announced: List[int] = []
+
+    def _key(self, r: int, k: int) -> str:
+        return f"{self.prefix}/{r}/{k}"
+
+    def step(self, k: int = None) -> int:
+        """Announce step ``k`` (default: the step after the last one announced here) and return
+        it once every rank has announced it; raise RankFailure naming the first rank that has
+        not within timeout_s."""
+        k = self.steps + 1 if k is None else int(k)
+        self.store.set(self._key(self.rank, k), "1")
+        self._announced.append(k)
+        if len(self._announced) > 2:
+            self.store.delete_key(self._key(self.rank, self._announced.pop(0)))
+        deadline = time.monotonic() + self.timeout_s
+        for r in range(self.world):
+            key = self._key(r, k)
+            while not self.store.check([key]):
+                if time.monotonic() > deadline:
+                    raise RankFailure(f"rank {r} did not reach step {k} within {self.timeout_s:g} s "
+                                      f"(seen from rank {self.rank})")
+                time.sleep(self.poll_s)
+        self.steps = k
+        return k
 
 
 class PeerExchange:
@@ -125,11 +176,13 @@ class ShardedDecodeStep:
     call, tp_decode_step).  With ``exchange`` (the default) each layer is one sharded attention
     call that merges the ranks' partials inside its launch over NVLink; otherwise a local
     partial, an NCCL all-gather and tp_combine_partials.  The graph must be released
-    (``release()``) before the process group is destroyed."""
+    (``release()``) before the process group is destroyed.  With a ``monitor`` (StepMonitor) every
+    replay first checks on the host that all ranks have reached the step."""
 
     def __init__(self, layers: List[TurboPolarKVCacheRuntime], k_in, v_in, q_in, out, rank: int, world: int,
-                 group=None, exchange: bool = True):
+                 group=None, exchange: bool = True, monitor: "StepMonitor" = None):
         self.layers, self.rank, self.world, self.group = layers, rank, world, group
+        self.monitor = monitor
         self.last = rank == world - 1
         dev = q_in[0].device
         hq = q_in[0].shape[0] * q_in[0].shape[-2]
@@ -166,6 +219,8 @@ class ShardedDecodeStep:
         return self.partials[i]
 
     def replay(self) -> None:
+        if self.monitor is not None:
+            self.monitor.step()
         if self.last:
             graph._check_room(self.layers)
         self.graph.replay()
