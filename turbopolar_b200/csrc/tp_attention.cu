@@ -1225,32 +1225,45 @@ static void code_table(int bits, uint32_t* out) {
   }
 }
 
-static int g_num_sms = 0;
+// Launch configuration per device, worked out on the first call on that device and shared by
+// every host thread (one mutex): the SM count, the shared memory the page pass may use and
+// how much of it each page-pass variant has been allowed so far (cudaFuncSetAttribute acts on
+// the current device).
+constexpr int kModes = 3;
+constexpr int kMaxDevices = 64;
+struct DeviceCfg {
+  int sms = 0;
+  int ring_budget[kModes] = {};
+  int attr_bytes[kModes] = {};
+};
+static std::mutex g_cfg_mutex;
+static DeviceCfg g_cfg[kMaxDevices];
 
-static int num_sms() {
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    g_num_sms = n;
-  }
-  return g_num_sms;
+static DeviceCfg& device_cfg() {  // caller holds g_cfg_mutex
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return g_cfg[(dev >= 0 && dev < kMaxDevices) ? dev : 0];
 }
 
-// Dynamic shared memory the page pass may use: the opt-in per-block limit and, when the
-// registers allow a split-combine CTA beside a page-pass CTA on one SM (so it starts, and
-// finishes the dense tail, while the page pass runs), no more than leaves room for it.
-static int ring_budget(const void* page_pass) {
-  static const void* fns[4] = {};
-  static int budgets[4] = {};
-  int slot = 0;
-  while (slot < 3 && fns[slot] && fns[slot] != page_pass) ++slot;
-  int& budget = budgets[slot];
-  if (fns[slot] != page_pass) {
-    fns[slot] = page_pass;
-    budget = 0;
+static int num_sms() {
+  std::lock_guard<std::mutex> lock(g_cfg_mutex);
+  DeviceCfg& cfg = device_cfg();
+  if (cfg.sms == 0) {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cfg.sms = n;
   }
+  return cfg.sms;
+}
+
+// Dynamic shared memory the page pass (variant `mode`, kernel `page_pass`) may use: the opt-in
+// per-block limit and, when the registers allow a split-combine CTA beside a page-pass CTA on
+// one SM (so it starts, and finishes the dense tail, while the page pass runs), no more than
+// leaves room for it.
+static int ring_budget(int mode, const void* page_pass) {
+  std::lock_guard<std::mutex> lock(g_cfg_mutex);
+  int& budget = device_cfg().ring_budget[mode];
   if (budget == 0) {
     int dev = 0, per_sm = 233472, per_block = 232448, reserved = 1024, regs = 65536;
     cudaGetDevice(&dev);
@@ -1268,6 +1281,22 @@ static int ring_budget(const void* page_pass) {
       budget = min(budget, per_sm - 2 * reserved - int(comb.sharedSizeBytes) - int(pp.sharedSizeBytes) - 256);
   }
   return budget;
+}
+
+// Let the page pass (variant `mode`) use `smem` bytes of dynamic shared memory on the current
+// device, and all of the unified L1/shared array as shared memory for it and the split
+// combine, so the split-combine CTAs fit beside a page-pass CTA.
+static cudaError_t reserve_smem(int mode, const void* page_pass, int smem) {
+  std::lock_guard<std::mutex> lock(g_cfg_mutex);
+  int& have = device_cfg().attr_bytes[mode];
+  if (smem <= have) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(page_pass, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(page_pass, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(split_combine_kernel),
+                             cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e == cudaSuccess) have = smem;
+  return e;
 }
 
 static int grid_size(int num_kv_heads, int num_q_heads) {
@@ -1405,25 +1434,16 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
                                           : reinterpret_cast<const void*>(decode_attention_kernel<kModeGeneral>);
   // Ring stages: as many as fit while a split-combine CTA still fits beside the page-pass CTA
   // on one SM (so it starts, and finishes the dense tail, while the page pass runs).
-  const int ring_bytes = ring_budget(fn) - P.smem_stage_off;
+  const int ring_bytes = ring_budget(mode, fn) - P.smem_stage_off;
   P.n_stages = min(kMaxStages, ring_bytes / P.stage_bytes) / kConsumers * kConsumers;
   if (P.n_stages < 2 * kConsumers)
     return fail(TP_ERR_UNSUPPORTED, "tp_decode_attention: not enough shared memory for the page ring");
   const int smem = P.smem_stage_off + P.n_stages * P.stage_bytes;
-  static int attr_bytes[3] = {0, 0, 0};
-  int& have = attr_bytes[mode];
-  if (smem > have) {
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    // All of the unified L1/shared array as shared memory, so the split-combine CTAs fit beside
-    // a page-pass CTA and start (and finish the dense tail) while the page pass runs.
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(split_combine_kernel),
-                               cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  {
+    const cudaError_t e = reserve_smem(mode, fn, smem);
     if (e != cudaSuccess)
       return fail(TP_ERR_CUDA, std::string("tp_decode_attention: cannot reserve ") + std::to_string(smem) +
                                    " bytes of shared memory: " + cudaGetErrorString(e));
-    have = smem;
   }
   {
     CallBuffers b;
