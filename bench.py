@@ -133,7 +133,6 @@ class ClockSampler:
 # ----------------------------------------------------------------------------- CPU baseline
 def _cpu_head_attention(args):
     """Oracle attention for the query heads of one KV head over its compressed pages."""
-    import numpy as np_
     from oracle import attention as oatt
     pages, fmt, q, scale = args
     k, v = oatt.decode_pages(pages, fmt)

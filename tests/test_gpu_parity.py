@@ -6,7 +6,7 @@ import torch
 
 import inputs
 from _util import ATOL, fmt_of, kv_inputs, oracle_attention, oracle_cache
-from oracle import polar, runtime as oruntime, vquant
+from oracle import polar, vquant
 
 pytestmark = pytest.mark.gpu
 

@@ -25,7 +25,6 @@ import torch.distributed as dist
 
 from . import _lib, graph
 from .cache import TurboPolarKVCacheRuntime
-from .pages import PAGE
 
 
 def page_range(n_pages: int, rank: int, world: int) -> Tuple[int, int]:
