@@ -332,7 +332,7 @@ def run_gpu(args):
     roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs", "kernel": "decode_attention_kernel",
             "launch_us": kern_us, "algorithmic_bytes_per_launch": launch_bytes,
-            "bytes_per_context_token": HKV * 296}
+            "bytes_per_context_token": HKV * 296, "frac_of_8000_spec": achieved / 8000.0}
     if dep_us is not None:
         roof["dependent_launch_us"] = dep_us
         roof["dependent_frac"] = launch_bytes / (dep_us * 1e-6) / 1e9 / peak
