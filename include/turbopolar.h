@@ -8,8 +8,10 @@
  *
  *   - Plain pointers and sizes only.  Device pointers are CUDA global-memory addresses on
  *     the current device; `stream` is a cudaStream_t passed as void*.
- *   - Nothing allocates: every buffer (page pools, tail, state words, workspace, outputs)
- *     belongs to the caller.  Every launch is asynchronous on `stream`.
+ *   - Nothing allocates except tp_ipc_alloc, the one allocation helper (it creates a
+ *     sequence-sharding exchange buffer that other processes map; it is called once at set-up,
+ *     never on the decode path): every buffer (page pools, tail, state words, workspace,
+ *     outputs) belongs to the caller.  Every launch is asynchronous on `stream`.
  *   - The return value is a tp_status; on failure tp_last_error() returns a message for
  *     the calling thread.  TP_ERR_INVALID maps to Python ValueError, TP_ERR_UNSUPPORTED to
  *     NotImplementedError, TP_ERR_CUDA to RuntimeError.
@@ -198,11 +200,20 @@ int tp_decode_step(const tp_page_pool* pool, const tp_tail* tail, int32_t* d_sta
  * TP_ERR_INVALID.  The first call on a device resolves the array's address with that device
  * current, so make it before capturing a stream.  Every call on a device shares the one
  * array: calls whose executions overlap on the GPU (concurrent streams) race and must be
- * serialised by the caller.  Allocates nothing (no cudaMalloc / cudaFree). */
+ * serialised by the caller.  Allocates nothing (no cudaMalloc / cudaFree).  Each call clears
+ * the array's error word (word 0) before it launches; tp_noalloc_error reads it back. */
 int tp_decode_attention_noalloc(const tp_page_pool* pool, const tp_tail* tail, tp_state state,
                                 const int32_t* d_state, const void* q, int32_t q_dtype,
                                 int32_t num_q_heads, float scale, void* out, float* partial_out,
                                 void* stream);
+
+/* The error word of the last tp_decode_attention_noalloc call on the current device: 0, or 1
+ * when a stage wait ran out (the output of that call is unusable).  Waits for `stream`, then
+ * copies the word into *error_out.  The word plays the part that workspace word 0 plays for
+ * tp_decode_attention, whose caller owns the workspace and can read it; a no-allocation caller
+ * has no handle on the array, and the next call clears the word.  Allocates nothing.  No
+ * counterpart in the reference. */
+int tp_noalloc_error(int32_t* error_out, void* stream);
 
 /* Merge n_parts partial records per query head, laid out [n_parts][H_q][TP_PARTIAL_FLOATS]
  * (the all-gathered output of tp_decode_attention on each sequence shard), into fp16

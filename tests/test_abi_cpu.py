@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 def test_version_and_row_bytes(lib):
     from turbopolar_b200 import _lib
-    assert lib.tp_version() == 2
+    assert lib.tp_version() == 3
     cases = {  # (l1_bits, deep_bits, split_dim) -> (l1_row, deep_row); test_turbo_polar_offline.py:26-34
         (4, 4, 64): (16, 16), (4, 8, 0): (0, 64), (8, 2, 32): (16, 12), (4, 8, 128): (32, 0), (4, 2, 2): (1, 16),
     }

@@ -38,10 +38,11 @@ static CallBuffers call(size_t base, size_t q, size_t out, bool step) {
   return b;
 }
 
-static bool run(StreamLog& log, const void* stream, const CallBuffers& b) {
+static bool run(StreamLog& log, const void* stream, const CallBuffers& b, int device = 0, uint64_t capture = 0,
+                uint64_t thread = 0) {
   Spans r, w;
   call_spans(b, r, w);
-  return log.independent(stream, r, w);
+  return log.independent(StreamKey{device, uintptr_t(stream), thread, capture}, r, w);
 }
 
 #define CHECK(cond) do { if (!(cond)) { std::printf("FAIL line %d: %s\n", __LINE__, #cond); std::exit(1); } } while (0)
@@ -49,9 +50,10 @@ static bool run(StreamLog& log, const void* stream, const CallBuffers& b) {
 int main() {
   const void* s1 = &mem[0];
   const void* s2 = &mem[1];
-  {  // the first call on a stream; then layers of a decode step (other caches, queries, outputs)
+  {  // the first call on a stream waits; then layers of a decode step (other caches, queries,
+     // outputs) stream early
     StreamLog log;
-    CHECK(run(log, s1, call(0, 300000, 400000, true)));
+    CHECK(!run(log, s1, call(0, 300000, 400000, true)));
     CHECK(run(log, s1, call(100000, 310000, 410000, true)));
     CHECK(run(log, s1, call(200000, 320000, 420000, true)));
   }
@@ -59,6 +61,15 @@ int main() {
     StreamLog log;
     run(log, s1, call(0, 300000, 400000, true));
     CHECK(!run(log, s1, call(0, 310000, 410000, true)));
+  }
+  {  // a call is compared with every call since the last one that waited, not only the previous
+     // one: steps on caches A, B, C, then A again (A's step may not have completed yet)
+    StreamLog log;
+    run(log, s1, call(0, 300000, 400000, true));
+    CHECK(run(log, s1, call(100000, 310000, 410000, true)));
+    CHECK(run(log, s1, call(200000, 320000, 420000, true)));
+    CHECK(!run(log, s1, call(0, 330000, 430000, true)));
+    CHECK(run(log, s1, call(100000, 340000, 440000, false)));  // the chain restarted at A's step
   }
   {  // a decode step, then plain attention on the same cache: it reads what the step wrote
     StreamLog log;
@@ -70,7 +81,7 @@ int main() {
     run(log, s1, call(0, 300000, 400000, false));
     CHECK(run(log, s1, call(0, 310000, 410000, false)));
   }
-  {  // the query is the previous call's output, whole or in part
+  {  // the query is an earlier call's output, whole or in part
     StreamLog log;
     run(log, s1, call(0, 300000, 400000, false));
     CHECK(!run(log, s1, call(100000, 400000, 410000, false)));
@@ -93,9 +104,40 @@ int main() {
   }
   {  // streams are logged separately
     StreamLog log;
+    run(log, s2, call(500000, 350000, 450000, true));
     run(log, s1, call(0, 300000, 400000, true));
     CHECK(run(log, s2, call(0, 310000, 410000, true)));
     CHECK(!run(log, s1, call(0, 320000, 420000, true)));
+  }
+  {  // one handle (the legacy default stream, 0) on two devices names two streams: a step on
+     // device 1 must not replace device 0's entry, or device 0's next step on the same cache
+     // would be judged independent of its previous one
+    StreamLog log;
+    const void* s0 = nullptr;
+    run(log, s0, call(0, 300000, 400000, true), 0);
+    run(log, s0, call(500000, 310000, 410000, true), 1);
+    CHECK(!run(log, s0, call(0, 320000, 420000, true), 0));
+    CHECK(run(log, s0, call(600000, 330000, 430000, true), 1));
+    CHECK(!run(log, s0, call(500000, 340000, 440000, true), 1));
+  }
+  {  // the per-thread default stream handle names one stream per host thread
+    StreamLog log;
+    run(log, s1, call(0, 300000, 400000, true), 0, 0, 11);
+    run(log, s1, call(100000, 310000, 410000, true), 0, 0, 12);
+    CHECK(!run(log, s1, call(0, 320000, 420000, true), 0, 0, 11));
+    CHECK(run(log, s1, call(200000, 330000, 430000, true), 0, 0, 12));
+  }
+  {  // a capture starts its own chain (its first call waits), leaves the eager chain alone, and
+     // replaces the stream's earlier captures
+    StreamLog log;
+    run(log, s1, call(0, 300000, 400000, true));
+    CHECK(!run(log, s1, call(0, 310000, 410000, true), 0, 7));  // first call of capture 7
+    CHECK(run(log, s1, call(100000, 320000, 420000, true), 0, 7));
+    CHECK(!run(log, s1, call(0, 330000, 430000, true), 0, 7));  // same cache inside capture 7
+    CHECK(!run(log, s1, call(0, 340000, 440000, true)));        // eager: the eager chain's step
+    const size_t before = log.size();
+    CHECK(!run(log, s1, call(100000, 350000, 450000, true), 0, 8));  // capture 8 replaces 7
+    CHECK(log.size() == before);
   }
   {  // sharded calls: one exchange per layer overlaps, a shared exchange does not
     StreamLog log;
@@ -107,6 +149,17 @@ int main() {
     CallBuffers c = call(200000, 320000, 420000, true);
     c.exchange = at(700000); c.exchange_bytes = 70000;
     CHECK(!run(log, s1, c));
+  }
+  {  // a chain longer than the log holds makes the next call wait and restarts the chain
+    StreamLog log;
+    run(log, s1, call(0, 300000, 400000, false));
+    int waited = 0;
+    for (int i = 0; i < 2 * ChainWrites::kMaxChain; ++i) {
+      CallBuffers b = call(0, 300000, 400000 + 16 * (i % 4096), false);
+      b.out_bytes = 16;
+      if (!run(log, s1, b)) ++waited;
+    }
+    CHECK(waited >= 1 && waited <= 2);
   }
   {  // more ranges than fit count as overlapping everything
     Spans r, w;

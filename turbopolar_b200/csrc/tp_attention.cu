@@ -35,7 +35,9 @@
 #include <cfloat>
 #include <cstring>
 #include <cmath>
+#include <functional>
 #include <mutex>
+#include <thread>
 
 #include "tp_codec.cuh"
 #include "tp_overlap.h"
@@ -925,15 +927,24 @@ __device__ __noinline__ float3 flush_partial(const AttnParams& P, CombineSmem& s
 }
 
 // ----------------------------------------------------------------------------- cross-GPU exchange
-// Exchange buffer of one rank: records [world][H_q][kExchWords] of 64-bit words written by every
-// rank into every rank's buffer (peer stores over NVLink), then this rank's epoch word and
+// Exchange buffer of one rank: records [2][world][H_q][kExchWords] of 64-bit words written by
+// every rank into every rank's buffer (peer stores over NVLink), then this rank's epoch word and
 // ticket.  A word holds one float of a record (m, l, o[128]) in its low half and the call's
 // epoch in its high half, so a reader knows a word is current from the word alone: an
 // aligned 64-bit store is single-copy atomic, and no fence or flag is needed between the
 // data and its validity (one one-way NVLink trip instead of store, release fence, flag store).
+//
+// The records of epoch e go to slot e & 1.  With one slot, a rank that finished reading epoch e
+// could publish e + 1 over its epoch-e record in a slower rank's buffer before that rank had
+// read it, and the slower rank would wait until its budget ran out.  With two, a rank writes
+// slot e & 1 again only at epoch e + 2, after it has read every rank's epoch e + 1 record; a
+// rank publishes e + 1 only after its epoch-e merge has completed (consecutive calls on one
+// exchange never overlap: the split combine of e + 1 starts its exchange after the page pass of
+// e + 1 has completed, which waited for the split combine of e to complete), so by then every
+// rank has finished reading slot e & 1.
 constexpr int kExchWords = TP_PARTIAL_FLOATS;
 __host__ __device__ inline size_t x_epoch_off(int world, int hq) {
-  return (size_t(world) * hq * kExchWords * sizeof(uint64_t) + 255) & ~size_t(255);
+  return (2 * size_t(world) * hq * kExchWords * sizeof(uint64_t) + 255) & ~size_t(255);
 }
 
 __device__ __forceinline__ void st_word_sys(uint64_t* p, float v, uint32_t epoch) {
@@ -953,9 +964,10 @@ __device__ __forceinline__ bool exchange_merge(const AttnParams& P, int qh, int 
   const int tid = threadIdx.x;
   const int W = P.xworld, hq = P.num_q_heads;
   const uint32_t ep = uint32_t(epoch);
+  const size_t slot = size_t(ep & 1u) * W;  // first record of this epoch's slot, in records of H_q
   if (tid < kD) {
     for (int r = 0; r < W; ++r) {
-      uint64_t* rec = reinterpret_cast<uint64_t*>(P.xbuf[r]) + (size_t(P.xrank) * hq + qh) * kExchWords;
+      uint64_t* rec = reinterpret_cast<uint64_t*>(P.xbuf[r]) + ((slot + P.xrank) * hq + qh) * kExchWords;
       st_word_sys(rec + 2 + tid, O, ep);
       if (tid == 0) {
         st_word_sys(rec, M, ep);
@@ -969,7 +981,7 @@ __device__ __forceinline__ bool exchange_merge(const AttnParams& P, int qh, int 
   if (tid < kD) {
     // Each thread reads the (m, l, o[tid]) words of every rank's record once they carry this
     // epoch (m first: the merge needs the maximum before the weights).
-    const uint64_t* base = reinterpret_cast<const uint64_t*>(P.xbuf[P.xrank]) + size_t(qh) * kExchWords;
+    const uint64_t* base = reinterpret_cast<const uint64_t*>(P.xbuf[P.xrank]) + (slot * hq + qh) * kExchWords;
     float m[TP_MAX_RANKS], l[TP_MAX_RANKS], o[TP_MAX_RANKS];
     bool ok = true;
     const long long t0 = clock64();
@@ -1307,6 +1319,23 @@ static int grid_size(int num_kv_heads, int num_q_heads) {
 
 static StreamLog g_stream_log;  // last call's writes per stream (tp_overlap.h)
 
+// The stream a launch on `s` goes to, as StreamLog tells streams apart: the current device, the
+// handle, the host thread for the per-thread default stream, and the capture being recorded.
+static StreamKey stream_key(cudaStream_t s) {
+  StreamKey k{};
+  cudaGetDevice(&k.device);
+  k.stream = reinterpret_cast<uintptr_t>(s);
+  if (s == cudaStreamPerThread) k.thread = uint64_t(std::hash<std::thread::id>{}(std::this_thread::get_id())) | 1u;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  unsigned long long id = 0;
+  if (cudaStreamGetCaptureInfo(s, &cs, &id) != cudaSuccess) {
+    cudaGetLastError();  // not capturing as far as the log is concerned; the launch reports errors
+  } else if (cs == cudaStreamCaptureStatusActive) {
+    k.capture = id ? id : 1;
+  }
+  return k;
+}
+
 }  // namespace tp
 
 using namespace tp;
@@ -1475,7 +1504,7 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
     }
     Spans reads, writes;
     call_spans(b, reads, writes);
-    P.spec = g_stream_log.independent(s, reads, writes) ? 1 : 0;
+    P.spec = g_stream_log.independent(stream_key(s), reads, writes) ? 1 : 0;
   }
   // The page pass is a programmatic dependent of whatever precedes it in the stream (a no-op
   // unless that kernel triggers early, as the split combine of a previous call does): its
@@ -1619,6 +1648,24 @@ static __device__ __align__(256) unsigned char g_noalloc_workspace[TP_NOALLOC_WO
 static std::mutex g_noalloc_mutex;
 static void* g_noalloc_ptr[64] = {};  // device address of the array, per device ordinal
 
+// Device address of the scratch array on the current device, resolved once per device with that
+// device current (the host-side name of the array is not a device address).
+static int noalloc_scratch(const char* who, void** ws) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string(who) + ": " + cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(TP_ERR_UNSUPPORTED, std::string(who) + ": device ordinal above 63");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_workspace);
+    if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string(who) + ": cudaGetSymbolAddress: " + cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *ws = g_noalloc_ptr[dev];
+  return TP_OK;
+}
+
 int tp_decode_attention_noalloc(const tp_page_pool* pool, const tp_tail* tail, tp_state state, const int32_t* d_state,
                                 const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
                                 float* partial_out, void* stream) {
@@ -1629,29 +1676,28 @@ int tp_decode_attention_noalloc(const tp_page_pool* pool, const tp_tail* tail, t
     return fail(TP_ERR_INVALID, "tp_decode_attention_noalloc: this head layout needs " + std::to_string(need) +
                                     " bytes of scratch, above the fixed " +
                                     std::to_string(sizeof(g_noalloc_workspace)) + "-byte maximum");
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_decode_attention_noalloc: ") + cudaGetErrorString(e));
-  if (dev < 0 || dev >= 64) return fail(TP_ERR_UNSUPPORTED, "tp_decode_attention_noalloc: device ordinal above 63");
   void* ws = nullptr;
-  {
-    // The host-side name of the array is not a device address; resolve it once per device,
-    // with that device current.
-    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (!g_noalloc_ptr[dev]) {
-      void* p = nullptr;
-      e = cudaGetSymbolAddress(&p, g_noalloc_workspace);
-      if (e != cudaSuccess)
-        return fail(TP_ERR_CUDA, std::string("tp_decode_attention_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-      g_noalloc_ptr[dev] = p;
-    }
-    ws = g_noalloc_ptr[dev];
-  }
+  const int st = noalloc_scratch("tp_decode_attention_noalloc", &ws);
+  if (st != TP_OK) return st;
   // Word 0 of the scratch is the sticky stage-wait error word; start this call from zero.
-  e = cudaMemsetAsync(ws, 0, sizeof(int), static_cast<cudaStream_t>(stream));
+  const cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(int), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_decode_attention_noalloc: ") + cudaGetErrorString(e));
   return tp_decode_attention(pool, tail, state, d_state, q, q_dtype, num_q_heads, scale, out, partial_out, ws,
                              sizeof(g_noalloc_workspace), stream);
+}
+
+int tp_noalloc_error(int32_t* error_out, void* stream) {
+  if (!error_out) return fail(TP_ERR_INVALID, "tp_noalloc_error: error_out is NULL");
+  void* ws = nullptr;
+  const int st = noalloc_scratch("tp_noalloc_error", &ws);
+  if (st != TP_OK) return st;
+  int32_t word = 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(&word, ws, sizeof(word), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_noalloc_error: ") + cudaGetErrorString(e));
+  *error_out = word;
+  return TP_OK;
 }
 
 int tp_combine_partials(const float* partials, int32_t n_parts, int32_t num_q_heads, void* out, void* stream) {

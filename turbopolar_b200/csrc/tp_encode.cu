@@ -160,7 +160,7 @@ extern "C" {
 
 const char* tp_last_error(void) { return g_last_error.c_str(); }
 
-int tp_version(void) { return 2; }
+int tp_version(void) { return 3; }
 
 int tp_row_bytes(const tp_format* fmt, int32_t* l1_row_bytes, int32_t* deep_row_bytes) {
   if (!fmt) return fail(TP_ERR_INVALID, "format is NULL");

@@ -7,7 +7,8 @@
 #include <cstddef>
 #include <cstdint>
 #include <mutex>
-#include <unordered_map>
+#include <map>
+#include <vector>
 
 namespace tp {
 
@@ -88,26 +89,98 @@ inline void call_spans(const CallBuffers& b, Spans& reads, Spans& writes) {
   writes.add(b.exchange, b.exchange_bytes);
 }
 
-// The last call's writes per stream.  Only this library's kernels let a dependent grid start
-// before they complete (griddepcontrol.launch_dependents), and any other kernel launched between
-// two calls starts after the first has completed, so the one call to compare with is the
-// previous one of this library on the same stream; work on other streams is ordered by events,
-// which wait for completion.
+// The writes a new call on a stream must not read early.  Only this library's kernels let a
+// dependent grid start before they complete (griddepcontrol.launch_dependents), and any other
+// kernel launched between two calls starts after the first has completed; work on other streams
+// is ordered by events, which wait for completion.  A call that streams early (independent)
+// starts once the previous call's split combine has started, which may be before that call, and
+// every independent call before it back to the last call that waited, have completed; so the
+// log keeps the union of the writes of every call since (and including) the last one that was
+// judged dependent.  A dependent call's page pass waits for its predecessor to complete before
+// it lets the next call start, so the union restarts there.  A stream's first call (no entry)
+// is judged dependent.
+//
+// A stream is identified by (device, handle, host thread, capture):
+//   - the device, because the legacy default stream (handle 0) and the per-thread default
+//     stream are per-device streams behind one handle value;
+//   - the host thread for the per-thread default stream handle only, which names a different
+//     stream in every host thread;
+//   - the id of the stream capture the call is recorded into (0 outside capture).  Inside one
+//     capture the recorded order is the replay order, so every decision holds at each replay;
+//     the first call of a capture is judged dependent.  A stream records one capture at a time,
+//     so entries of its earlier captures are dropped when a new one starts.
+struct StreamKey {
+  int device;
+  uintptr_t stream;
+  uint64_t thread;   // 0 unless `stream` is the per-thread default stream handle
+  uint64_t capture;  // 0 outside stream capture
+  bool operator<(const StreamKey& o) const {
+    if (device != o.device) return device < o.device;
+    if (stream != o.stream) return stream < o.stream;
+    if (thread != o.thread) return thread < o.thread;
+    return capture < o.capture;
+  }
+};
+
+// Writes of a chain of calls.  More ranges than kMaxChain count as overlapping everything, so
+// an overflow can only make the next call wait (and restart the chain).
+struct ChainWrites {
+  static constexpr int kMaxChain = 1024;
+  std::vector<Span> s;
+  bool all = false;
+  void reset(const Spans& w) {
+    s.assign(w.s, w.s + w.n);
+    all = w.all;
+  }
+  void add(const Spans& w) {
+    if (w.all || s.size() + size_t(w.n) > size_t(kMaxChain)) {
+      all = true;
+      return;
+    }
+    s.insert(s.end(), w.s, w.s + w.n);
+  }
+  bool meets(const Spans& r) const {
+    if (all || r.all) return true;
+    for (const Span& a : s)
+      for (int j = 0; j < r.n; ++j)
+        if (a.lo < r.s[j].hi && r.s[j].lo < a.hi) return true;
+    return false;
+  }
+};
+
 class StreamLog {
  public:
-  // True when nothing the previous call on `stream` writes is read by this call; records this
-  // call's writes as the stream's last either way.
-  bool independent(const void* stream, const Spans& reads, const Spans& writes) {
+  // True when this call may read early: the stream has a chain and nothing its calls write is
+  // read by this call.  Adds this call's writes to the chain, or restarts the chain with them.
+  bool independent(const StreamKey& key, const Spans& reads, const Spans& writes) {
     std::lock_guard<std::mutex> lock(mu_);
-    const auto it = last_.find(stream);
-    const bool ok = it == last_.end() || !it->second.meets(reads);
-    last_[stream] = writes;
+    auto it = last_.find(key);
+    if (it == last_.end()) {
+      if (key.capture != 0) {
+        for (auto j = last_.begin(); j != last_.end();) {
+          const StreamKey& o = j->first;
+          if (o.device == key.device && o.stream == key.stream && o.thread == key.thread && o.capture != 0)
+            j = last_.erase(j);
+          else
+            ++j;
+        }
+      }
+      last_[key].reset(writes);
+      return false;
+    }
+    const bool ok = !it->second.meets(reads);
+    if (ok) it->second.add(writes);
+    else it->second.reset(writes);
     return ok;
+  }
+  size_t size() {
+    std::lock_guard<std::mutex> lock(mu_);
+    return last_.size();
   }
 
  private:
   std::mutex mu_;
-  std::unordered_map<const void*, Spans> last_;
+  std::map<StreamKey, ChainWrites> last_;
 };
 
 }  // namespace tp
