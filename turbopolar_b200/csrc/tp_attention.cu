@@ -102,10 +102,14 @@ struct AttnParams {
   int stage_bytes, off_vcodes, off_codes, off_vscales;  // a stage holds one unit as laid out in the pool
   int smem_bar_off, smem_lut_off, smem_merge_off, smem_stage_off;
   int smem_scale_off;  // float radius scale of the unit in each ring stage (int8 radii)
-  int smem_rlut_off;   // per compute warp: float16 exp(code * scale) for the 256 int8 codes
+  int smem_tab_off;    // adapter format: the deep (cos, sin) table, 16 copies
   int n_stages;  // ring stages of the page pass
-  uint32_t lut[2 * kLutEntries];  // half2 (cos, sin) per code: level-1 [0, 256), deep [256, 512)
-  int lut_deep;                   // shared-memory copy: level-1 entries, then deep from here
+  int lut_deep;  // shared-memory float2 (cos, sin) tables: level-1 entries, then deep from here
+  // Decoder tables computed on the host (code / (2^bits - 1) * 2pi - pi in float32, cos and sin
+  // rounded to float32; decoder.py:36-56): the fast path's 16 entries as float16 hi / lo parts
+  // (uint2 (cos_hi, sin_hi), (cos_lo, sin_lo)) in the first 16 slots, or the adapter path's 256
+  // deep entries as float2.  The general path builds its tables on the device.
+  float2 cs[kLutEntries];
 };
 
 // Work partition: the U units (half pages, head-major, uph per head) are cut into C = min(U,
@@ -219,9 +223,18 @@ __device__ __forceinline__ void softmax_update(WarpAcc& A, float (&sc)[NT][4], f
 }
 
 // ----------------------------------------------------------------------------- key decode
-// Fast path: default format (level-1 and deep both 4-bit, split_dim 64, float16 radii).
-// Writes the 16 decoded pairs [16t, 16t+16) of stage row `r` as half2 (x, y).
-__device__ __forceinline__ void decode_row_fast(const uint8_t* stage, const AttnParams& P, const uint32_t* lut,
+// Every path decodes a key pair as the reference decoder does (decoder.py:57-67): the float32
+// radius times the float32 (cos, sin) of the code angle, each product rounded once to float16,
+// so the keys the kernel multiplies are the reference's decoded keys.
+//
+// Fast path: default format (level-1 and deep both 4-bit, split_dim 64, float16 radii).  Entry
+// c of `cs` holds the float32 cos and sin of code c split into float16 parts, .x = (cos_hi,
+// sin_hi) and .y = (cos_lo, sin_lo) with hi = fp16(v) and lo = fp16(v - hi).  A pair is
+// fma(r, hi, r * lo) in half2: one rounding of r * (hi + lo), and hi + lo carries the float32
+// value to about 2^-22, so the key is fp16(r * cos) as the reference decodes it, except when
+// r * cos lies within that distance of a float16 rounding boundary.  Writes the 16 decoded
+// pairs [16t, 16t+16) of stage row `r` as half2 (x, y).
+__device__ __forceinline__ void decode_row_fast(const uint8_t* stage, const AttnParams& P, const uint2* cs,
                                                 int r, int t, uint32_t (&kp)[16]) {
   const uint4 R0 = lds128(stage + swz128(r, 2 * t));
   const uint4 R1 = lds128(stage + swz128(r, 2 * t + 1));
@@ -231,32 +244,33 @@ __device__ __forceinline__ void decode_row_fast(const uint8_t* stage, const Attn
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const uint32_t cw = (i < 8) ? C.x : C.y;
-    const int sh = 4 * (i & 7);
-    const uint32_t cs = lut[(cw >> sh) & 15u];
+    const uint2 e = cs[(cw >> (4 * (i & 7))) & 15u];
     const __half2 rp = u32_as_h2(rw[i >> 1]);
-    kp[i] = h2_as_u32(__hmul2((i & 1) ? __high2half2(rp) : __low2half2(rp), u32_as_h2(cs)));
+    const __half2 rr = (i & 1) ? __high2half2(rp) : __low2half2(rp);
+    kp[i] = h2_as_u32(__hfma2(rr, u32_as_h2(e.x), __hmul2(rr, u32_as_h2(e.y))));
   }
 }
 
-// General path: any supported format.  LUTs: level-1 at lut[0..255], deep at lut[256..511].
-__device__ __forceinline__ void decode_row_general(const uint8_t* stage, const AttnParams& P, const uint32_t* lut,
+// General path: any supported format.  Tables: level-1 at cs[0..], deep at cs[P.lut_deep..].
+__device__ __forceinline__ void decode_row_general(const uint8_t* stage, const AttnParams& P, const float2* cs,
                                                    float radius_scale, int r, int t, uint32_t (&kp)[16]) {
   const uint8_t* l1row = stage + P.off_codes + r * P.code_row;
   const uint8_t* deeprow = l1row + P.l1_row;
 #pragma unroll 4
   for (int i = 0; i < 16; ++i) {
     const int j = 16 * t + i;
-    uint32_t code, cs;
+    uint32_t code;
+    float2 c;
     if (j < P.l1_pairs) {
       if (P.l1_bits == 8) code = l1row[j];
       else code = (l1row[j >> 1] >> (4 * (j & 1))) & 15u;
-      cs = lut[code];
+      c = cs[code];
     } else {
       const int rel = j - P.l1_pairs;
       if (P.deep_bits == 8) code = deeprow[rel];
       else if (P.deep_bits == 4) code = (deeprow[rel >> 1] >> (4 * (rel & 1))) & 15u;
       else code = (deeprow[rel >> 2] >> (2 * (rel & 3))) & 3u;
-      cs = lut[P.lut_deep + code];
+      c = cs[P.lut_deep + code];
     }
     float rad;
     if (P.int8_radii) {
@@ -265,25 +279,31 @@ __device__ __forceinline__ void decode_row_general(const uint8_t* stage, const A
     } else {
       rad = __half2float(reinterpret_cast<const __half*>(stage + swz128(r, j >> 3))[j & 7]);
     }
-    const __half2 h = u32_as_h2(cs);
-    kp[i] = pack_h2(rad * __low2float(h), rad * __high2float(h));
+    kp[i] = pack_h2(rad * c.x, rad * c.y);
   }
 }
 
 // Adapter path: log-int8 radii, split_dim 0 and 8-bit angle codes (the format the Llama
-// adapter uses, benchmarks/turbopolar_fast_attention.py:217-228).  rlut holds float16
-// exp(c * scale) for the 256 int8 codes of this unit's page (index c + 128).
-__device__ __forceinline__ void decode_row_adapter(const uint8_t* stage, const AttnParams& P, const uint32_t* lut,
-                                                   const __half* rlut, int r, int t, uint32_t (&kp)[16]) {
+// adapter uses, benchmarks/turbopolar_fast_attention.py:217-228).  Radius of int8 code c:
+// exp(c * scale) = 2^(c * s2) with s2 = scale * log2(e) (decoder.py:57-63), in float32 (the code
+// as a float by the 2^23 bias trick, one ex2 per pair).  The (cos, sin) of the 8-bit angle code
+// come from a 256-entry float2 table held 16 times, copy j at float2 index 16 * c + j: lane l
+// reads copy l % 16, so each half warp's 64-bit lookups hit 16 different bank pairs.
+__device__ __forceinline__ void decode_row_adapter(const uint8_t* stage, const AttnParams& P, const float2* tab,
+                                                   float s2, int r, int t, uint32_t (&kp)[16]) {
   const uint4 R = lds128(stage + r * kPairs + 16 * t);
   const uint4 C = lds128(stage + P.off_codes + r * kPairs + 16 * t);
-  const uint32_t rw[4] = {R.x, R.y, R.z, R.w}, cw[4] = {C.x, C.y, C.z, C.w};
-  const uint32_t* dl = lut + P.lut_deep;
+  // Radius codes as unsigned bytes c + 128 (two's complement with the sign bit flipped).
+  const uint32_t rw[4] = {R.x ^ 0x80808080u, R.y ^ 0x80808080u, R.z ^ 0x80808080u, R.w ^ 0x80808080u};
+  const uint32_t cw[4] = {C.x, C.y, C.z, C.w};
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    const uint32_t rb = (rw[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-    const uint32_t cb = (cw[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-    kp[i] = h2_as_u32(__hmul2(__half2half2(rlut[rb ^ 0x80u]), u32_as_h2(dl[cb])));
+    // 0x4B0000xx is the float 2^23 + xx: minus 2^23 + 128 leaves the signed code exactly.
+    const float code = __uint_as_float(prmt(rw[i >> 2], 0x4B000000u, 0x7540u | uint32_t(i & 3))) - 8388736.f;
+    const float rad = exp2_approx(code * s2);
+    const uint32_t c = prmt(cw[i >> 2], 0u, 0x4440u | uint32_t(i & 3));
+    const float2 a = tab[c << 4];
+    kp[i] = pack_h2(rad * a.x, rad * a.y);
   }
 }
 
@@ -293,8 +313,8 @@ enum { kModeGeneral = 0, kModeFast = 1, kModeAdapter = 2 };
 
 // ----------------------------------------------------------------------------- one half page
 template <int kMode>
-__device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, const AttnParams& P, const uint32_t* lut,
-                                             const __half* rlut, const uint32_t (&qf)[16], float radius_scale,
+__device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, const AttnParams& P, const float2* lut,
+                                             const float2* tab, const uint32_t (&qf)[16], float radius_scale,
                                              int valid_tokens, int lane) {
   const int g = lane >> 2, t = lane & 3;
   float sc[2][4];
@@ -302,11 +322,12 @@ __device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, c
   for (int mt = 0; mt < 2; ++mt) {
     uint32_t k0[16], k1[16];
     if (kMode == kModeFast) {
-      decode_row_fast(stage, P, lut, 16 * mt + g, t, k0);
-      decode_row_fast(stage, P, lut, 16 * mt + g + 8, t, k1);
+      const uint2* cs = reinterpret_cast<const uint2*>(lut);
+      decode_row_fast(stage, P, cs, 16 * mt + g, t, k0);
+      decode_row_fast(stage, P, cs, 16 * mt + g + 8, t, k1);
     } else if (kMode == kModeAdapter) {
-      decode_row_adapter(stage, P, lut, rlut, 16 * mt + g, t, k0);
-      decode_row_adapter(stage, P, lut, rlut, 16 * mt + g + 8, t, k1);
+      decode_row_adapter(stage, P, tab, radius_scale, 16 * mt + g, t, k0);
+      decode_row_adapter(stage, P, tab, radius_scale, 16 * mt + g + 8, t, k1);
     } else {
       decode_row_general(stage, P, lut, radius_scale, 16 * mt + g, t, k0);
       decode_row_general(stage, P, lut, radius_scale, 16 * mt + g + 8, t, k1);
@@ -505,12 +526,14 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity) { retu
 // no wait is ever more than one phase ahead of its barrier.  A thread dispatches one bulk copy
 // at a time, so the copies are spread over lanes that never hold up the warps that compute;
 // consumers get the same number of units to within one.
+// At most 192 registers a thread: 8 warps of the page pass and 8 of the split combine (64 each)
+// then fit the SM's 64K registers together.
 template <int kMode>
-__global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __grid_constant__ AttnParams P) {
+__global__ void __maxnreg__(192) decode_attention_kernel(const __grid_constant__ AttnParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ tp_state s_pre;  // cache state as read before the wait, one read for the CTA
   __shared__ float s_wt[2][kMaxHeads][kConsumers + 1];  // merge weights, then the maximum
-  uint32_t* lut = reinterpret_cast<uint32_t*>(smem + P.smem_lut_off);
+  float2* lut = reinterpret_cast<float2*>(smem + P.smem_lut_off);
   float* merge = reinterpret_cast<float*>(smem + P.smem_merge_off);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.smem_bar_off);
   uint64_t* empty = full + kMaxStages;
@@ -530,11 +553,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   // Before the previous kernel in the stream has completed (this grid is its programmatic
   // dependent): the code tables, the ring barriers and the first copies, none of which
   // depends on anything that kernel writes.
-  {
-    const int n1 = 1 << P.l1_bits, n2 = 1 << P.deep_bits;
-    for (int i = tid; i < n1 + n2; i += kThreads) {
-      lut[i] = P.lut[i < n1 ? i : kLutEntries + (i - n1)];
+  if (kMode == kModeAdapter) {
+    // Entry c of the deep table, 16 copies (float2 index 16 * c + j): a warp-uniform parameter
+    // load, stored by lanes 0-15.
+    float2* tab = reinterpret_cast<float2*>(smem + P.smem_tab_off);
+    for (int c = warp; c < kLutEntries; c += kThreads / 32) {
+      const float2 v = P.cs[c];
+      if (lane < 16) tab[16 * c + lane] = v;
     }
+  } else if (kMode == kModeFast) {
+    if (tid < 16) lut[tid] = P.cs[tid];
+  } else {
+    const int n1 = 1 << P.l1_bits, n2 = 1 << P.deep_bits;
+    for (int i = tid; i < n1 + n2; i += kThreads)
+      lut[i] = i < n1 ? cos_sin_of_code(i, P.l1_bits) : cos_sin_of_code(i - n1, P.deep_bits);
   }
   auto init_barriers = [&]() {
     for (int st = 0; st < R; ++st) {
@@ -628,7 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
   } else {
     WarpAcc A;
     uint32_t qf[16];
-    __half* rlut = reinterpret_cast<__half*>(smem + P.smem_rlut_off) + warp * 256;
+    const float2* tab = reinterpret_cast<const float2*>(smem + P.smem_tab_off) + (lane & 15);
     int cur = -1;        // segment of the accumulator (-1: none yet)
     int kvh = 0, gc = gmax;
     // Ring stage and phase of this warp's next unit.
@@ -650,18 +682,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const __g
       if (ready) {
         const int64_t pos0 = (int64_t(st.first_page) + u.y) * kPage + u.z * kHalf;
         const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, kHalf));
-        const float rs = P.int8_radii ? stage_scale[slot] : 0.f;
-        if (kMode == kModeAdapter) {
-          // float16 exp(c * scale) of every int8 code c of this unit's page (decoder.py:57-63);
-          // the previous unit's reads of the table ended at the __syncwarp that closed it.
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int cidx = lane + 32 * k;
-            rlut[cidx] = __float2half_rn(__expf(float(cidx - 128) * rs));
-          }
-          __syncwarp();
-        }
-        process_half<kMode>(A, ring + slot * P.stage_bytes, P, lut, rlut, qf, rs, vt, lane);
+        // The adapter path takes the radius scale in base-2 units.
+        const float rs = P.int8_radii ? stage_scale[slot] * (kMode == kModeAdapter ? 1.4426950408889634f : 1.f) : 0.f;
+        process_half<kMode>(A, ring + slot * P.stage_bytes, P, lut, tab, qf, rs, vt, lane);
       } else {
         timed_out = true;  // the unit is left out; the error word marks the result unusable
       }
@@ -842,6 +865,7 @@ struct SmemPage {
   uint8_t codes[kPage * kPairs];  // encode scratch: one code per pair
   float red[8];                   // encode scratch: block reduction
   __align__(16) uint8_t block[kMaxPageBytes];
+  float2 cs[2 * kLutEntries];     // float32 (cos, sin) per code: level-1 [0, 256), deep [256, 512)
   __half radii_scale;
 };
 
@@ -866,32 +890,33 @@ __device__ __forceinline__ float4 page_token(const AttnParams& P, SmemPage& pg, 
     return make_float4(vx[0], vx[1], vx[2], vx[3]);
   }
   float kx[4];
-  const uint32_t* lut = P.lut;
+  const float2* lut = pg.cs;
   const uint8_t* row = codes_at(W, pg.block, t);
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
     const int j = 2 * lane + e;
-    uint32_t code, cs;
+    uint32_t code;
+    float2 c2;
     if (j < P.l1_pairs) {
       code = P.l1_bits == 8 ? row[j] : (row[j >> 1] >> (4 * (j & 1))) & 15u;
-      cs = lut[code];
+      c2 = lut[code];
     } else {
       const uint8_t* drow = row + P.l1_row;
       const int rel = j - P.l1_pairs;
       if (P.deep_bits == 8) code = drow[rel];
       else if (P.deep_bits == 4) code = (drow[rel >> 1] >> (4 * (rel & 1))) & 15u;
       else code = (drow[rel >> 2] >> (2 * (rel & 3))) & 3u;
-      cs = lut[kLutEntries + code];
+      c2 = lut[kLutEntries + code];
     }
     float r;
     if (P.int8_radii) {
-      r = expf(float(*radius_i8_at(W, pg.block, t, j)) * __half2float(pg.radii_scale));
+      const float arg = __fmul_rn(float(*radius_i8_at(W, pg.block, t, j)), __half2float(pg.radii_scale));
+      r = d2f(exp(double(arg)));
     } else {
       r = __half2float(*radius_f16_at(W, pg.block, t, j));
     }
-    const float2 c2 = __half22float2(u32_as_h2(cs));
-    kx[2 * e] = __half2float(__float2half_rn(r * c2.x));
-    kx[2 * e + 1] = __half2float(__float2half_rn(r * c2.y));
+    kx[2 * e] = __half2float(__float2half_rn(__fmul_rn(r, c2.x)));
+    kx[2 * e + 1] = __half2float(__float2half_rn(__fmul_rn(r, c2.y)));
   }
   return make_float4(kx[0], kx[1], kx[2], kx[3]);
 }
@@ -916,6 +941,11 @@ __device__ __noinline__ float3 flush_partial(const AttnParams& P, CombineSmem& s
   SmemPage& pg = sm.page;
   const T* tk = static_cast<const T*>(P.tail_k) + int64_t(kvh) * kPage * kD;
   const T* tv = static_cast<const T*>(P.tail_v) + int64_t(kvh) * kPage * kD;
+  // Decoder tables for page_token (the encode's closing barrier orders them before the reads).
+  for (int i = threadIdx.x; i < 2 * kLutEntries; i += blockDim.x) {
+    const int bits = i < kLutEntries ? P.l1_bits : P.deep_bits, code = i & (kLutEntries - 1);
+    pg.cs[i] = code < (1 << bits) ? cos_sin_of_code(code, bits) : make_float2(0.f, 0.f);
+  }
   encode_page<T>(tk, tv, kD, P.wpool, pg.block, &pg.radii_scale, pg.codes, pg.red,
                  static_cast<const T*>(P.k_new) + int64_t(kvh) * P.new_head_stride,
                  static_cast<const T*>(P.v_new) + int64_t(kvh) * P.new_head_stride);
@@ -1221,22 +1251,6 @@ __global__ void combine_kernel(const float* partials, int n_parts, int num_q_hea
   out[int64_t(h) * kD + d] = __float2half_rn(L > 0.f ? O / L : 0.f);
 }
 
-// half2 (cos, sin) of the decoder angle of every code value, the angle evaluated in float32
-// exactly as rfsn_v11/quant/polar/decoder.py:36-56 does (code / (2^bits - 1) * 2pi - pi, each
-// op rounded to float32; the double evaluation below rounds to the same floats), cos and sin
-// correctly rounded to float32, then to float16.
-static void code_table(int bits, uint32_t* out) {
-  const int lm1 = (1 << bits) - 1;
-  for (int code = 0; code <= lm1; ++code) {
-    const float norm = float(double(code) / double(lm1));
-    const float prod = float(double(norm) * double(6.28318530717958647692f));
-    const float ang = float(double(prod) - double(3.14159265358979323846f));
-    const __half c = __float2half_rn(float(cos(double(ang))));
-    const __half s = __float2half_rn(float(sin(double(ang))));
-    out[code] = uint32_t(__half_as_ushort(c)) | (uint32_t(__half_as_ushort(s)) << 16);
-  }
-}
-
 // Launch configuration per device, worked out on the first call on that device and shared by
 // every host thread (one mutex): the SM count, the shared memory the page pass may use and
 // how much of it each page-pass variant has been allowed so far (cudaFuncSetAttribute acts on
@@ -1315,6 +1329,36 @@ static int grid_size(int num_kv_heads, int num_q_heads) {
   const int group = num_q_heads / num_kv_heads;
   const int nqc = (group + kMaxHeads - 1) / kMaxHeads;
   return max(num_sms(), num_kv_heads * nqc);
+}
+
+// float32 (cos, sin) of the decoder angle of a `bits`-bit code, on the host: the angle is
+// evaluated as rfsn_v11/quant/polar/decoder.py:36-56 does (code / (2^bits - 1) * 2pi - pi, each op
+// rounded to float32; evaluating in double and rounding gives the same floats), cos and sin in
+// double rounded to float32 -- the values cos_sin_of_code gives on the device.
+static float2 host_cos_sin(int code, int bits) {
+  const int lm1 = (1 << bits) - 1;
+  const float norm = float(double(code) / double(lm1));
+  const float prod = float(double(norm) * double(6.28318530717958647692f));
+  const float ang = float(double(prod) - double(3.14159265358979323846f));
+  return make_float2(float(cos(double(ang))), float(sin(double(ang))));
+}
+
+// The launch's host-side decoder table for `mode` (AttnParams::cs).
+static void fill_decoder_table(int mode, float2* cs) {
+  for (int i = 0; i < kLutEntries; ++i) cs[i] = make_float2(0.f, 0.f);
+  if (mode == kModeFast) {
+    for (int c = 0; c < 16; ++c) {
+      const float2 v = host_cos_sin(c, 4);
+      const __half ch = __float2half_rn(v.x), sh = __float2half_rn(v.y);
+      const __half cl = __float2half_rn(v.x - __half2float(ch)), sl = __float2half_rn(v.y - __half2float(sh));
+      uint2 e;
+      e.x = uint32_t(__half_as_ushort(ch)) | (uint32_t(__half_as_ushort(sh)) << 16);
+      e.y = uint32_t(__half_as_ushort(cl)) | (uint32_t(__half_as_ushort(sl)) << 16);
+      std::memcpy(&cs[c], &e, sizeof(e));
+    }
+  } else if (mode == kModeAdapter) {
+    for (int c = 0; c < kLutEntries; ++c) cs[c] = host_cos_sin(c, 8);
+  }
 }
 
 static StreamLog g_stream_log;  // last call's writes per stream (tp_overlap.h)
@@ -1409,9 +1453,6 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
   P.nqc = (P.group + kMaxHeads - 1) / kMaxHeads;
   P.gmax = P.group < kMaxHeads ? P.group : kMaxHeads;
   P.scale_log2 = scale * 1.4426950408889634f;
-  for (int i = 0; i < 2 * kLutEntries; ++i) P.lut[i] = 0u;
-  code_table(P.l1_bits, P.lut);
-  code_table(P.deep_bits, P.lut + kLutEntries);
   P.out = static_cast<__half*>(out);
   P.partial_out = partial_out;
   const int grid = grid_size(hkv, num_q_heads);
@@ -1449,14 +1490,15 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
   P.smem_bar_off = 0;                       // full and empty barrier per ring stage
   P.smem_lut_off = up(2 * kMaxStages * 8, 128);
   P.lut_deep = 1 << P.l1_bits;
-  P.smem_merge_off = P.smem_lut_off + up(4 * ((1 << P.l1_bits) + (1 << P.deep_bits)), 128);
+  P.smem_merge_off = P.smem_lut_off + up(8 * ((1 << P.l1_bits) + (1 << P.deep_bits)), 128);
   P.smem_scale_off = up(P.smem_merge_off + merge_bytes, 128);
-  P.smem_rlut_off = P.smem_scale_off + up(kMaxStages * 4, 128);
+  P.smem_tab_off = P.smem_scale_off + up(kMaxStages * 4, 128);
   const int mode = (P.l1_bits == 4 && P.deep_bits == 4 && pool->fmt.split_dim == 64 && !P.int8_radii) ? kModeFast
                    : (P.int8_radii && pool->fmt.split_dim == 0 && P.deep_bits == 8)                 ? kModeAdapter
                                                                                                    : kModeGeneral;
-  P.smem_stage_off = up(P.smem_rlut_off + (mode == kModeAdapter ? kConsumers * 256 * 2 : 0), 128);
+  P.smem_stage_off = up(P.smem_tab_off + (mode == kModeAdapter ? kLutEntries * 16 * 8 : 0), 128);
 
+  fill_decoder_table(mode, P.cs);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const void* fn = mode == kModeFast      ? reinterpret_cast<const void*>(decode_attention_kernel<kModeFast>)
                    : mode == kModeAdapter ? reinterpret_cast<const void*>(decode_attention_kernel<kModeAdapter>)

@@ -19,6 +19,16 @@ constexpr int kMaxUnitBytes = kUnit * 128 + kVCodesUnit + kUnit * 64 + kVScalesU
 constexpr int kMaxPageBytes = 2 * kMaxUnitBytes;
 
 // ----------------------------------------------------------------------------- codec math
+// float32 (cos, sin) of the decoder angle of a `bits`-bit code: code / (2^bits - 1) * 2pi - pi
+// with each op rounded to float32 (rfsn_v11/quant/polar/decoder.py:36-56), cos and sin
+// evaluated in float64 and rounded to float32.
+__device__ __forceinline__ float2 cos_sin_of_code(int code, int bits) {
+  const int lm1 = (1 << bits) - 1;
+  const float norm = __fdiv_rn(float(code), float(lm1));
+  const float ang = __fsub_rn(__fmul_rn(norm, 6.28318530717958647692f), 3.14159265358979323846f);
+  return make_float2(d2f(cos(double(ang))), d2f(sin(double(ang))));
+}
+
 struct PairCode {
   __half r;     // float16 radius
   float norm;   // normalised angle in [0, 1] (float32, the promoted value)

@@ -32,14 +32,8 @@ static RefView ref_view(const tp_block_store& r) {
 __device__ void build_cos_sin(float2* tab, int l1_bits, int deep_bits) {
   for (int i = threadIdx.x; i < 512; i += blockDim.x) {
     const int bits = i < 256 ? l1_bits : deep_bits;
-    const int code = i & 255, lm1 = (1 << bits) - 1;
-    float2 v = make_float2(0.f, 0.f);
-    if (code <= lm1) {
-      const float norm = __fdiv_rn(float(code), float(lm1));
-      const float ang = __fsub_rn(__fmul_rn(norm, 6.28318530717958647692f), 3.14159265358979323846f);
-      v = make_float2(d2f(cos(double(ang))), d2f(sin(double(ang))));
-    }
-    tab[i] = v;
+    const int code = i & 255;
+    tab[i] = code < (1 << bits) ? cos_sin_of_code(code, bits) : make_float2(0.f, 0.f);
   }
 }
 
