@@ -15,6 +15,7 @@ import pytest
 import torch
 
 import inputs
+from _util import ATOL, fmt_of, oracle_attention
 
 ADAPTER_FMT = dict(use_int8_radii=True, k_angle_bits_deep=8, split_dim=0)
 
@@ -108,12 +109,20 @@ def test_fast_cache_decode_sequence_vs_reference(name, golden, golden_meta):
     cache = TurboPolarFastCache(cfg)
     qs, ks, vs = inputs.adapter_inputs()
     want = golden[f"adapter/{name}/out"]
+    k_all = np.concatenate(list(ks), 2)
+    v_all = np.concatenate(list(vs), 2)
+    err_ref = err_oracle = 0.0
     for i in range(qs.shape[0]):
         out = cache.decode_attention(torch.from_numpy(qs[i]).to(dev), torch.from_numpy(ks[i]).to(dev),
                                      torch.from_numpy(vs[i]).to(dev), cfg.attention_scale)
         assert out.shape == (1, 4, 128) and out.dtype == torch.float16
-        err = np.max(np.abs(out.float().cpu().numpy().astype(np.float64) - want[i].astype(np.float64)))
-        assert err < 3e-3, (i, err)  # the reference reduces in float16
+        got = out.float().cpu().numpy().astype(np.float64)
+        exact = oracle_attention(qs[i][0, :, 0], k_all[:, :, :i + 1], v_all[:, :, :i + 1], fmt_of(cfg),
+                                 cfg.use_int8_radii, cfg.attention_scale)
+        err_oracle = max(err_oracle, float(np.max(np.abs(got[0] - exact))))
+        err_ref = max(err_ref, float(np.max(np.abs(got - want[i].astype(np.float64)))))
+    assert err_oracle < ATOL, err_oracle               # float64 oracle on the same tokens
+    assert err_ref < 3e-3, (err_ref, err_oracle)      # the reference adapter reduces in float16
     assert cache.offset == qs.shape[0]
     assert cache.runtime.get_io_telemetry() == pytest.approx(golden_meta[f"adapter/{name}"]["telemetry"])
     assert cache.nbytes == golden_meta[f"adapter/{name}"]["telemetry"]["actual_cache_bytes"]

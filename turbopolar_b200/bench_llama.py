@@ -5,14 +5,23 @@
 The model is the Llama-3.2-1B architecture with 128-channel heads (hidden 2048, 32 query / 8
 KV heads x head_dim 128, FFN 8192, vocabulary 128256, RMSNorm, RoPE theta 500000) built by
 Hugging Face ``transformers`` from a config, weights ~ N(0, 0.02) in fp16 (seeded; no
-checkpoint).  The prompt is uniform random token ids (seed 3).  The dense run prefills the
-prompt and decodes ``--new`` tokens greedily; the TurboPolar run (``patch_llama_attention`` +
-``make_turbo_caches``: prefill through decompress-on-read, decode through the fused CUDA kernel)
-is fed the same tokens (teacher forcing), so the logits of every step compare one to one under
-the reference's gate (``rfsn_v11/candidates/turbo_polar_adapter.py:97-105``).  Tokens/s is the
-decode phase of each run after a short warm-up run (CUDA events around the token loop; Python
-dispatch and the reference's per-append finiteness check included).
-Prints one JSON line.
+checkpoint).  The prompt is uniform random token ids (seed 3) and is prefilled by the Hugging
+Face forward: with a ``DynamicCache`` (dense), or with ``patch_llama_attention`` +
+``make_turbo_caches`` (TurboPolar: append, then decompress-on-read of the history, as the
+reference adapter's ``update_and_fetch`` does).  Decode steps then run as one CUDA graph per
+step (``llama_graph.LlamaDecodeGraph``: projections, RoPE, attention, MLP and logits of all
+layers in one replay).  Three runs:
+
+* dense: static fp16 cache + SDPA, greedy; its tokens drive the other two (teacher forcing);
+* fused: the TurboPolar cache, one ``tp_decode_step`` (append + fused attention) per layer;
+* format only: the TurboPolar cache, each layer appending the token and attending in float32
+  over the cache decoded by ``tp_decode_pages`` plus the dense tail (eager) -- the key and
+  value formats' error without the fused kernel's arithmetic.
+
+The logits of every step of fused and format-only are compared with the dense run's under the
+reference's gate (``rfsn_v11/candidates/turbo_polar_adapter.py:97-105``), and fused with format
+only directly.  Tokens/s is the graph-replayed decode loop of each captured run (CUDA events,
+host launch of one replay and one token copy per step included).  Prints one JSON line.
 """
 
 from __future__ import annotations
@@ -66,25 +75,11 @@ def logit_gate(base: np.ndarray, cand: np.ndarray) -> dict:
     return m
 
 
-def run(model, prompt: torch.Tensor, new: int, cache, forced=None):
-    """Prefill, then `new` decode steps (greedy, or the `forced` tokens).  Returns the logits of
-    the prefill's last position and of every decode step, the tokens, and decode seconds."""
-    logits, tokens = [], []
+def prefill(model, prompt: torch.Tensor, cache):
+    """Hugging Face forward over the prompt into ``cache``; the last position's float32 logits."""
     with torch.no_grad():
         out = model(input_ids=prompt, past_key_values=cache, use_cache=True)
-        last = out.logits[:, -1].float()
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for t in range(new):
-            logits.append(last)
-            nxt = last.argmax(-1, keepdim=True) if forced is None else forced[:, t:t + 1]
-            tokens.append(nxt)
-            out = model(input_ids=nxt, past_key_values=cache, use_cache=True)
-            last = out.logits[:, -1].float()
-        e.record()
-        torch.cuda.synchronize()
-    return torch.cat(logits).cpu().numpy(), torch.cat(tokens, dim=1), s.elapsed_time(e) / 1e3
+    return out.logits[:, -1].float()
 
 
 def main(argv=None):
@@ -96,31 +91,93 @@ def main(argv=None):
     a = ap.parse_args(argv)
     from transformers import DynamicCache
     from . import build, llama
+    from .llama_graph import LlamaDecodeGraph
     build.build()
     dev = torch.device("cuda:0")
-    # The dense baseline's attention: torch SDPA without the cuDNN backend, which builds a new
-    # execution plan for every new key length (each decode step) and would time that instead.
     torch.backends.cuda.enable_cudnn_sdp(False)
     model = build_model(a.layers, a.vocab, dev)
     rng = np.random.default_rng(3)
     prompt = torch.from_numpy(rng.integers(0, a.vocab, size=(1, a.prompt))).to(dev)
+    max_len = a.prompt + a.new + 64
+    n = a.new
 
-    run(model, prompt[:, :64], 4, DynamicCache())  # warm-up (kernel selection, allocator)
-    base, toks, t_dense = run(model, prompt, a.new, DynamicCache())
-    llama.patch_llama_attention(model)
-    try:
-        run(model, prompt[:, :64], 4, llama.make_turbo_caches(a.layers, 32, 8, 128), forced=toks)  # warm-up
-        caches = llama.make_turbo_caches(a.layers, 32, 8, 128)
-        cand, _, t_turbo = run(model, prompt, a.new, caches, forced=toks)
-    finally:
-        llama.unpatch_llama_attention(model)
+    def turbo_caches():
+        llama.patch_llama_attention(model)
+        try:
+            caches = llama.make_turbo_caches(a.layers, 32, 8, 128, device=dev, max_seq_len=max_len,
+                                             check_finite=False)
+            first = prefill(model, prompt, caches)
+        finally:
+            llama.unpatch_llama_attention(model)
+        return caches, first
+
+    # Dense: greedy; its tokens drive the TurboPolar runs.
+    dcache = DynamicCache()
+    first_dense = prefill(model, prompt, dcache)
+    dense = LlamaDecodeGraph(model, dcache, max_len)
+    del dcache
+    dense.capture()
+    base = torch.empty((n, a.vocab), dtype=torch.float32, device=dev)
+    base[0].copy_(first_dense[0])
+    tok0 = first_dense.argmax(-1, keepdim=True)
+    steps_logits = torch.empty((n, a.vocab), dtype=torch.float32, device=dev)
+    tokens = torch.empty((1, n), dtype=torch.long, device=dev)
+    tokens[:, 0:1] = tok0
+    # Greedy: step t's argmax is the input of step t + 1 (recorded for the forced runs).
+    dense.token.copy_(tok0)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for t in range(n):
+        dense.step()
+        steps_logits[t].copy_(dense.logits[0])
+        if t + 1 < n:
+            tokens[:, t + 1:t + 2] = dense.next
+            dense.token.copy_(dense.next)
+    end.record()
+    torch.cuda.synchronize()
+    t_dense = start.elapsed_time(end) / 1e3
+    base[1:].copy_(steps_logits[:n - 1])
+    dense.release()
+    del dense
+    torch.cuda.empty_cache()
+
+    # Fused TurboPolar decode, teacher-forced on the dense tokens.
+    caches, first_turbo = turbo_caches()
+    fused = LlamaDecodeGraph(model, caches, max_len)
+    fused.capture()
+    cand = torch.empty_like(base)
+    cand[0].copy_(first_turbo[0])
+    t_turbo = fused.decode(tokens[:, :1], n, forced=tokens, logits_out=steps_logits)
+    cand[1:].copy_(steps_logits[:n - 1])
+    device_errors = sum(layer.runtime.read_device_error() for layer in caches.layers)
+    kv_bytes_turbo = int(sum(c.nbytes for c in caches.layers))
+    fused.release()
+    del fused, caches
+    torch.cuda.empty_cache()
+
+    # Format only: the same cache contents attended in float32 over the decoded pages.
+    caches, first_fmt = turbo_caches()
+    fmt = LlamaDecodeGraph(model, caches, max_len, attention="decompressed")
+    only = torch.empty_like(base)
+    only[0].copy_(first_fmt[0])
+    fmt.decode(tokens[:, :1], n, forced=tokens, logits_out=steps_logits)
+    only[1:].copy_(steps_logits[:n - 1])
+    del fmt, caches
+
+    b, c_, o = base.cpu().numpy(), cand.cpu().numpy(), only.cpu().numpy()
     dense_bytes = a.layers * 2 * 8 * 128 * 2 * (a.prompt + a.new)
     line = {
         "workload": f"random-init Llama ({a.layers} layers, hidden 2048, 32q/8kv x 128, FFN 8192, vocab {a.vocab})",
-        "prompt_tokens": a.prompt, "decode_tokens": a.new, "dtype": "f16", "data": "synthetic (seeded ids)",
-        "dense_tokens_per_s": a.new / t_dense, "turbopolar_tokens_per_s": a.new / t_turbo,
-        "kv_bytes_dense": dense_bytes, "kv_bytes_turbopolar": int(sum(c.nbytes for c in caches)),
-        "logits": logit_gate(base, cand),
+        "prompt_tokens": a.prompt, "decode_tokens": n, "dtype": "f16", "data": "synthetic (seeded ids)",
+        "decode": "one CUDA graph replay per token (all layers), greedy dense run; TurboPolar runs fed its tokens",
+        "dense_tokens_per_s": n / t_dense, "turbopolar_tokens_per_s": n / t_turbo,
+        "kv_bytes_dense": dense_bytes, "kv_bytes_turbopolar": kv_bytes_turbo,
+        "logits_fused_vs_dense": logit_gate(b, c_),
+        "logits_format_only_vs_dense": logit_gate(b, o),
+        "logits_fused_vs_format_only": {"max_abs_logit_delta": float(np.abs(c_ - o).max()),
+                                        "mean_abs_logit_delta": float(np.abs(c_ - o).mean()),
+                                        "greedy_agreement": float(np.mean(c_.argmax(-1) == o.argmax(-1)))},
+        "device_errors": device_errors,
     }
     print(json.dumps(line), flush=True)
 

@@ -39,10 +39,16 @@ class TurboPolarFastCache(CacheLayerMixin):
     is_compileable = False
     is_sliding = False
 
-    def __init__(self, config: TurboPolarConfig, device=None, max_seq_len: Optional[int] = None):
+    def __init__(self, config: TurboPolarConfig, device=None, max_seq_len: Optional[int] = None,
+                 check_finite: bool = True):
         super().__init__()
         self.config = config
-        self.runtime = TurboPolarKVCacheRuntime(config, device=device, max_seq_len=max_seq_len)
+        # check_finite keeps the reference's finiteness check on every append
+        # (turbo_polar_cache.py:69-70), one host synchronisation per layer and token; without it
+        # nothing on the decode path synchronises (runtime.read_device_error() reads the
+        # device's error word when the caller chooses to).
+        self.runtime = TurboPolarKVCacheRuntime(config, device=device, max_seq_len=max_seq_len,
+                                                check_finite=check_finite)
         self.bridge = CudaKernelBridge()
         self.decoder = PolarQuantDecoder()
         self.v_dequantizer = GroupedVQuantizer(group_size=32)
@@ -159,7 +165,7 @@ class TurboPolarCache(Cache):
 
 
 def make_turbo_caches(num_layers: int, num_q_heads: int, num_kv_heads: int, head_dim: int, use_qjl: bool = False,
-                      device=None, max_seq_len: Optional[int] = None) -> TurboPolarCache:
+                      device=None, max_seq_len: Optional[int] = None, check_finite: bool = True) -> TurboPolarCache:
     """Per-layer caches with the adapter's benchmark format (int8 log radii, 8-bit deep
     angles, every pair in the deep level)."""
     if head_dim not in (64, 128):
@@ -176,8 +182,8 @@ def make_turbo_caches(num_layers: int, num_q_heads: int, num_kv_heads: int, head
         k_angle_bits_deep=8,
         split_dim=0,
     )
-    return TurboPolarCache([TurboPolarFastCache(config, device=device, max_seq_len=max_seq_len)
-                            for _ in range(num_layers)])
+    return TurboPolarCache([TurboPolarFastCache(config, device=device, max_seq_len=max_seq_len,
+                                                check_finite=check_finite) for _ in range(num_layers)])
 
 
 def _is_standard_causal_mask(mask: Optional[torch.Tensor], seq_len: int, cache_len: int) -> bool:
