@@ -228,23 +228,29 @@ __device__ __forceinline__ void softmax_update(WarpAcc& A, float (&sc)[NT][4], f
 // so the keys the kernel multiplies are the reference's decoded keys.
 //
 // Fast path: default format (level-1 and deep both 4-bit, split_dim 64, float16 radii).  Entry
-// c of `cs` holds the float32 cos and sin of code c split into float16 parts, .x = (cos_hi,
-// sin_hi) and .y = (cos_lo, sin_lo) with hi = fp16(v) and lo = fp16(v - hi).  A pair is
-// fma(r, hi, r * lo) in half2: one rounding of r * (hi + lo), and hi + lo carries the float32
-// value to about 2^-22, so the key is fp16(r * cos) as the reference decodes it, except when
-// r * cos lies within that distance of a float16 rounding boundary.  Writes the 16 decoded
-// pairs [16t, 16t+16) of stage row `r` as half2 (x, y).
-__device__ __forceinline__ void decode_row_fast(const uint8_t* stage, const AttnParams& P, const uint2* cs,
+// c of the table at shared address tab_sa (256-byte aligned) holds the float32 cos and sin of
+// code c split into float16 parts, (cos_hi, sin_hi) then (cos_lo, sin_lo), hi = fp16(v) and
+// lo = fp16(v - hi).  A pair is fma(r, hi, r * lo) in half2: one rounding of r * (hi + lo), and
+// hi + lo carries the float32 value to about 2^-22, so the key is fp16(r * cos) as the reference
+// decodes it, except when r * cos lies within that distance of a float16 rounding boundary.
+// Entry addresses: each code byte's nibbles are pre-scaled by 8 in place (two masks per four
+// bytes), and one byte permute splices a scaled nibble into the table's address.  Writes the 16
+// decoded pairs [16t, 16t+16) of stage row `r` as half2 (x, y).
+__device__ __forceinline__ void decode_row_fast(const uint8_t* stage, const AttnParams& P, uint32_t tab_sa,
                                                 int r, int t, uint32_t (&kp)[16]) {
   const uint4 R0 = lds128(stage + swz128(r, 2 * t));
   const uint4 R1 = lds128(stage + swz128(r, 2 * t + 1));
-  // Row r's codes: 16 level-1 bytes then 16 deep bytes; lane t takes bytes [8t, 8t + 8).
   const uint2 C = lds64(stage + P.off_codes + r * 32 + 8 * t);
   const uint32_t rw[8] = {R0.x, R0.y, R0.z, R0.w, R1.x, R1.y, R1.z, R1.w};
+  const uint32_t lo[2] = {(C.x << 3) & 0x78787878u, (C.y << 3) & 0x78787878u};
+  const uint32_t hi[2] = {(C.x >> 1) & 0x78787878u, (C.y >> 1) & 0x78787878u};
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    const uint32_t cw = (i < 8) ? C.x : C.y;
-    const uint2 e = cs[(cw >> (4 * (i & 7))) & 15u];
+    const int n = i & 7;
+    const uint32_t src = (n & 1) ? hi[i >> 3] : lo[i >> 3];
+    const uint32_t addr = prmt(src, tab_sa, 0x7650u | uint32_t(n >> 1));  // tab_sa + 8 * nibble
+    uint2 e;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(e.x), "=r"(e.y) : "r"(addr));
     const __half2 rp = u32_as_h2(rw[i >> 1]);
     const __half2 rr = (i & 1) ? __high2half2(rp) : __low2half2(rp);
     kp[i] = h2_as_u32(__hfma2(rr, u32_as_h2(e.x), __hmul2(rr, u32_as_h2(e.y))));
@@ -322,9 +328,9 @@ __device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, c
   for (int mt = 0; mt < 2; ++mt) {
     uint32_t k0[16], k1[16];
     if (kMode == kModeFast) {
-      const uint2* cs = reinterpret_cast<const uint2*>(lut);
-      decode_row_fast(stage, P, cs, 16 * mt + g, t, k0);
-      decode_row_fast(stage, P, cs, 16 * mt + g + 8, t, k1);
+      const uint32_t tab_sa = (smem_u32(lut) + 255u) & ~255u;
+      decode_row_fast(stage, P, tab_sa, 16 * mt + g, t, k0);
+      decode_row_fast(stage, P, tab_sa, 16 * mt + g + 8, t, k1);
     } else if (kMode == kModeAdapter) {
       decode_row_adapter(stage, P, tab, radius_scale, 16 * mt + g, t, k0);
       decode_row_adapter(stage, P, tab, radius_scale, 16 * mt + g + 8, t, k1);
@@ -562,7 +568,10 @@ __global__ void __maxnreg__(192) decode_attention_kernel(const __grid_constant__
       if (lane < 16) tab[16 * c + lane] = v;
     }
   } else if (kMode == kModeFast) {
-    if (tid < 16) lut[tid] = P.cs[tid];
+    if (tid < 16) {  // at the first 256-byte boundary of the table region (256 bytes of slack)
+      const uint32_t sa = (smem_u32(lut) + 255u) & ~255u;
+      reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(lut) + (sa - smem_u32(lut)))[tid] = P.cs[tid];
+    }
   } else {
     const int n1 = 1 << P.l1_bits, n2 = 1 << P.deep_bits;
     for (int i = tid; i < n1 + n2; i += kThreads)
@@ -1490,7 +1499,7 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
   P.smem_bar_off = 0;                       // full and empty barrier per ring stage
   P.smem_lut_off = up(2 * kMaxStages * 8, 128);
   P.lut_deep = 1 << P.l1_bits;
-  P.smem_merge_off = P.smem_lut_off + up(8 * ((1 << P.l1_bits) + (1 << P.deep_bits)), 128);
+  P.smem_merge_off = P.smem_lut_off + up(8 * ((1 << P.l1_bits) + (1 << P.deep_bits)), 128) + 256;
   P.smem_scale_off = up(P.smem_merge_off + merge_bytes, 128);
   P.smem_tab_off = P.smem_scale_off + up(kMaxStages * 4, 128);
   const int mode = (P.l1_bits == 4 && P.deep_bits == 4 && pool->fmt.split_dim == 64 && !P.int8_radii) ? kModeFast
