@@ -50,6 +50,12 @@ namespace tp {
 #ifndef TP_COPY_SPLIT
 #define TP_COPY_SPLIT 1
 #endif
+// TP_QK_CUDA_CORES=1 builds the comparison variant of the default-format page pass whose Q.K
+// product runs on CUDA cores (float32 FMA over the same decoded key fragments, quad shuffles;
+// P.V unchanged; at most 4 query heads per KV head) instead of mma.sync.  Off in the product.
+#ifndef TP_QK_CUDA_CORES
+#define TP_QK_CUDA_CORES 0
+#endif
 constexpr int kConsumers = TP_CONSUMERS;             // page-pass compute warps
 constexpr int kCopySplit = TP_COPY_SPLIT;            // copy-warp lanes (and bulk copies) per unit
 constexpr int kIssuers = kConsumers * kCopySplit;    // issuing lanes of the copy warp(s)
@@ -103,6 +109,7 @@ struct AttnParams {
   int smem_bar_off, smem_lut_off, smem_merge_off, smem_stage_off;
   int smem_scale_off;  // float radius scale of the unit in each ring stage (int8 radii)
   int smem_tab_off;    // adapter format: the deep (cos, sin) table, 16 copies
+  int smem_qcc_off;    // TP_QK_CUDA_CORES: float32 query heads per compute warp
   int n_stages;  // ring stages of the page pass
   int lut_deep;  // shared-memory float2 (cos, sin) tables: level-1 entries, then deep from here
   // Decoder tables computed on the host (code / (2^bits - 1) * 2pi - pi in float32, cos and sin
@@ -318,10 +325,19 @@ __device__ __forceinline__ void decode_row_adapter(const uint8_t* stage, const A
 enum { kModeGeneral = 0, kModeFast = 1, kModeAdapter = 2 };
 
 // ----------------------------------------------------------------------------- one half page
+// TP_QK_CUDA_CORES: float offset of key pair j's 4 query heads (float2 each) in a warp's query
+// copy, 4 floats of padding per 16 pairs so the 4 lanes of a quad hit different banks.
+__device__ __forceinline__ int qcc_off(int j) { return j * 8 + (j >> 4) * 4; }
+constexpr int kQccFloats = 528;
+
 template <int kMode>
 __device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, const AttnParams& P, const float2* lut,
                                              const float2* tab, const uint32_t (&qf)[16], float radius_scale,
-                                             int valid_tokens, int lane) {
+                                             int valid_tokens, int lane
+#if TP_QK_CUDA_CORES
+                                             , const float* qs
+#endif
+                                             ) {
   const int g = lane >> 2, t = lane & 3;
   float sc[2][4];
 #pragma unroll
@@ -338,6 +354,35 @@ __device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, c
       decode_row_general(stage, P, lut, radius_scale, 16 * mt + g, t, k0);
       decode_row_general(stage, P, lut, radius_scale, 16 * mt + g + 8, t, k1);
     }
+#if TP_QK_CUDA_CORES
+    if (kMode == kModeFast) {
+      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int j = 16 * t + i;
+        const float4 qa = *reinterpret_cast<const float4*>(qs + qcc_off(j));
+        const float4 qb = *reinterpret_cast<const float4*>(qs + qcc_off(j) + 4);
+        const float2 ka = __half22float2(u32_as_h2(k0[i])), kb = __half22float2(u32_as_h2(k1[i]));
+        s0[0] = fmaf(ka.x, qa.x, fmaf(ka.y, qa.y, s0[0])); s0[1] = fmaf(ka.x, qa.z, fmaf(ka.y, qa.w, s0[1]));
+        s0[2] = fmaf(ka.x, qb.x, fmaf(ka.y, qb.y, s0[2])); s0[3] = fmaf(ka.x, qb.z, fmaf(ka.y, qb.w, s0[3]));
+        s1[0] = fmaf(kb.x, qa.x, fmaf(kb.y, qa.y, s1[0])); s1[1] = fmaf(kb.x, qa.z, fmaf(kb.y, qa.w, s1[1]));
+        s1[2] = fmaf(kb.x, qb.x, fmaf(kb.y, qb.y, s1[2])); s1[3] = fmaf(kb.x, qb.z, fmaf(kb.y, qb.w, s1[3]));
+      }
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        s0[h] += __shfl_xor_sync(0xffffffffu, s0[h], 1);
+        s0[h] += __shfl_xor_sync(0xffffffffu, s0[h], 2);
+        s1[h] += __shfl_xor_sync(0xffffffffu, s1[h], 1);
+        s1[h] += __shfl_xor_sync(0xffffffffu, s1[h], 2);
+      }
+      // The mma accumulator layout: rows g, g + 8; heads 2t, 2t + 1 (heads >= 4 are zero).
+      sc[mt][0] = t == 0 ? s0[0] : (t == 1 ? s0[2] : 0.f);
+      sc[mt][1] = t == 0 ? s0[1] : (t == 1 ? s0[3] : 0.f);
+      sc[mt][2] = t == 0 ? s1[0] : (t == 1 ? s1[2] : 0.f);
+      sc[mt][3] = t == 0 ? s1[1] : (t == 1 ? s1[3] : 0.f);
+      continue;
+    }
+#endif
     float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int ks = 0; ks < 8; ks += 2) {
@@ -533,9 +578,14 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity) { retu
 // at a time, so the copies are spread over lanes that never hold up the warps that compute;
 // consumers get the same number of units to within one.
 // At most 192 registers a thread: 8 warps of the page pass and 8 of the split combine (64 each)
-// then fit the SM's 64K registers together.
+// then fit the SM's 64K registers together (the CUDA-core comparison variant needs more).
+#if TP_QK_CUDA_CORES
+#define TP_PAGE_PASS_REGS 255
+#else
+#define TP_PAGE_PASS_REGS 192
+#endif
 template <int kMode>
-__global__ void __maxnreg__(192) decode_attention_kernel(const __grid_constant__ AttnParams P) {
+__global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __grid_constant__ AttnParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ tp_state s_pre;  // cache state as read before the wait, one read for the CTA
   __shared__ float s_wt[2][kMaxHeads][kConsumers + 1];  // merge weights, then the maximum
@@ -670,6 +720,9 @@ __global__ void __maxnreg__(192) decode_attention_kernel(const __grid_constant__
     WarpAcc A;
     uint32_t qf[16];
     const float2* tab = reinterpret_cast<const float2*>(smem + P.smem_tab_off) + (lane & 15);
+#if TP_QK_CUDA_CORES
+    float* qcc = reinterpret_cast<float*>(smem + P.smem_qcc_off) + warp * kQccFloats;
+#endif
     int cur = -1;        // segment of the accumulator (-1: none yet)
     int kvh = 0, gc = gmax;
     // Ring stage and phase of this warp's next unit.
@@ -684,6 +737,21 @@ __global__ void __maxnreg__(192) decode_attention_kernel(const __grid_constant__
         kvh = vh / P.nqc;
         gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
         load_q_frags(P, kvh * P.group + chunk * kMaxHeads, gc, lane, qf);
+#if TP_QK_CUDA_CORES
+        {  // float32 copy of the chunk's query heads for the CUDA-core Q.K
+          const int qh0 = kvh * P.group + chunk * kMaxHeads;
+          for (int jj = lane; jj < kPairs; jj += 32)
+            for (int h = 0; h < 4; ++h) {
+              float2 v = make_float2(0.f, 0.f);
+              if (h < gc) {
+                const __half* qp = static_cast<const __half*>(P.q) + int64_t(qh0 + h) * kD + 2 * jj;
+                v = make_float2(__half2float(qp[0]), __half2float(qp[1]));
+              }
+              *reinterpret_cast<float2*>(qcc + qcc_off(jj) + 2 * h) = v;
+            }
+          __syncwarp();
+        }
+#endif
         acc_reset(A);
       }
       const int slot = warp * S + js;
@@ -693,7 +761,11 @@ __global__ void __maxnreg__(192) decode_attention_kernel(const __grid_constant__
         const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, kHalf));
         // The adapter path takes the radius scale in base-2 units.
         const float rs = P.int8_radii ? stage_scale[slot] * (kMode == kModeAdapter ? 1.4426950408889634f : 1.f) : 0.f;
-        process_half<kMode>(A, ring + slot * P.stage_bytes, P, lut, tab, qf, rs, vt, lane);
+        process_half<kMode>(A, ring + slot * P.stage_bytes, P, lut, tab, qf, rs, vt, lane
+#if TP_QK_CUDA_CORES
+                            , qcc
+#endif
+        );
       } else {
         timed_out = true;  // the unit is left out; the error word marks the result unusable
       }
@@ -1505,7 +1577,8 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
   const int mode = (P.l1_bits == 4 && P.deep_bits == 4 && pool->fmt.split_dim == 64 && !P.int8_radii) ? kModeFast
                    : (P.int8_radii && pool->fmt.split_dim == 0 && P.deep_bits == 8)                 ? kModeAdapter
                                                                                                    : kModeGeneral;
-  P.smem_stage_off = up(P.smem_tab_off + (mode == kModeAdapter ? kLutEntries * 16 * 8 : 0), 128);
+  P.smem_qcc_off = up(P.smem_tab_off + (mode == kModeAdapter ? kLutEntries * 16 * 8 : 0), 128);
+  P.smem_stage_off = up(P.smem_qcc_off + (TP_QK_CUDA_CORES ? kConsumers * kQccFloats * 4 : 0), 128);
 
   fill_decoder_table(mode, P.cs);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
