@@ -16,7 +16,9 @@ layers in one replay).  Three runs:
 * fused: the TurboPolar cache, one ``tp_decode_step`` (append + fused attention) per layer;
 * format only: the TurboPolar cache, each layer appending the token and attending in float32
   over the cache decoded by ``tp_decode_pages`` plus the dense tail (eager) -- the key and
-  value formats' error without the fused kernel's arithmetic.
+  value formats' error without the fused kernel's arithmetic;
+* dense, Hugging Face eager: the model's own forward (SDPA) on the same tokens, a second dense
+  float16 implementation whose agreement with the first is the rounding noise floor.
 
 The logits of every step of fused and format-only are compared with the dense run's under the
 reference's gate (``rfsn_v11/candidates/turbo_polar_adapter.py:97-105``), and fused with format
@@ -164,6 +166,18 @@ def main(argv=None):
     only[1:].copy_(steps_logits[:n - 1])
     del fmt, caches
 
+    # A second dense baseline: Hugging Face's own eager forward (SDPA attention) on the same tokens.
+    # Two dense float16 implementations differ only by rounding; their agreement is the noise floor
+    # the gate's thresholds meet on this model.
+    dcache = DynamicCache()
+    hf = torch.empty_like(base)
+    hf[0].copy_(prefill(model, prompt, dcache)[0])
+    with torch.no_grad():
+        for t in range(n - 1):
+            hf[t + 1].copy_(model(input_ids=tokens[:, t:t + 1], past_key_values=dcache, use_cache=True).logits[0, -1].float())
+    del dcache
+    h = hf.cpu().numpy()
+
     b, c_, o = base.cpu().numpy(), cand.cpu().numpy(), only.cpu().numpy()
     dense_bytes = a.layers * 2 * 8 * 128 * 2 * (a.prompt + a.new)
     line = {
@@ -177,6 +191,9 @@ def main(argv=None):
         "logits_fused_vs_format_only": {"max_abs_logit_delta": float(np.abs(c_ - o).max()),
                                         "mean_abs_logit_delta": float(np.abs(c_ - o).mean()),
                                         "greedy_agreement": float(np.mean(c_.argmax(-1) == o.argmax(-1)))},
+        "logits_dense_hf_eager_vs_dense": logit_gate(b, h),
+        "logits_fused_vs_dense_hf_eager": logit_gate(h, c_),
+        "logits_format_only_vs_dense_hf_eager": logit_gate(h, o),
         "device_errors": device_errors,
     }
     print(json.dumps(line), flush=True)

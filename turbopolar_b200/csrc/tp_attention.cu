@@ -56,6 +56,12 @@ namespace tp {
 #ifndef TP_QK_CUDA_CORES
 #define TP_QK_CUDA_CORES 0
 #endif
+// Key formats whose page pass computes P.V exactly (bit kMode set; see process_half): the
+// values dequantised as the reference rounds them, fp16(code * scale), and the softmax weights
+// as float16 hi + lo parts.  The others fold the value scale into float16 weights.
+#ifndef TP_EXACT_PV
+#define TP_EXACT_PV 4
+#endif
 constexpr int kConsumers = TP_CONSUMERS;             // page-pass compute warps
 constexpr int kCopySplit = TP_COPY_SPLIT;            // copy-warp lanes (and bulk copies) per unit
 constexpr int kIssuers = kConsumers * kCopySplit;    // issuing lanes of the copy warp(s)
@@ -183,7 +189,7 @@ __device__ __forceinline__ void acc_reset(WarpAcc& A) {
 }
 
 // Online-softmax update from the raw score fragments of NT 16-token tiles; returns P in sc.
-template <int NT>
+template <int NT, bool kOnes>
 __device__ __forceinline__ void softmax_update(WarpAcc& A, float (&sc)[NT][4], float c) {
   float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
@@ -217,10 +223,12 @@ __device__ __forceinline__ void softmax_update(WarpAcc& A, float (&sc)[NT][4], f
       A.o[i][0] *= al0; A.o[i][2] *= al0;
       A.o[i][1] *= al1; A.o[i][3] *= al1;
     }
+    if (kOnes) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      A.ones[i][0] *= al0; A.ones[i][2] *= al0;
-      A.ones[i][1] *= al1; A.ones[i][3] *= al1;
+      for (int i = 0; i < 4; ++i) {
+        A.ones[i][0] *= al0; A.ones[i][2] *= al0;
+        A.ones[i][1] *= al1; A.ones[i][3] *= al1;
+      }
     }
     A.m[0] = mn0;
     A.m[1] = mn1;
@@ -399,24 +407,54 @@ __device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, c
       if (16 * mt + g + 8 >= valid_tokens) sc[mt][2] = sc[mt][3] = -INFINITY;
     }
   }
-  softmax_update<2>(A, sc, P.scale_log2);
+  constexpr bool kExact = (TP_EXACT_PV >> kMode) & 1;
+  softmax_update<2, !kExact>(A, sc, P.scale_log2);
   const uint8_t* vcodes = stage + P.off_vcodes;
   const uint8_t* vscales = stage + P.off_vscales;
-  const uint32_t kOne = 0x3C003C00u;
+  const uint32_t K = 0x64646464u;  // float16 0x64xx = 1024 + xx: a byte permute makes code + 1152
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt) {
-    const uint32_t b0 = movmatrix_trans(pack_h2(sc[mt][0], sc[mt][1]));
-    const uint32_t b1 = movmatrix_trans(pack_h2(sc[mt][2], sc[mt][3]));
     // (scale[tok][G], scale[tok+1][G]) for this lane's token pairs (2t, 2t+1) and (2t+8, 2t+9).
     const uint4 S01 = lds128(vscales + mt * 128 + t * 32);
     const uint4 S89 = lds128(vscales + mt * 128 + t * 32 + 16);
     const uint32_t s01[4] = {S01.x, S01.y, S01.z, S01.w}, s89[4] = {S89.x, S89.y, S89.z, S89.w};
+    if (kExact) {
+      // Exact P.V.  V is dequantised on the A side as the reference dequantises it
+      // (v_quant/encoder.py:32-38: fp16(code * scale)): the biased code minus 1152 is the code
+      // exactly, and one float16 multiply by the token's scale rounds once.  P enters as float16
+      // hi + lo parts (hi = fp16(p), lo = fp16(p - hi)), two products per tile, so the weights
+      // carry about 22 bits; no bias tile is needed.
+      const uint32_t h0 = pack_h2(sc[mt][0], sc[mt][1]), h1 = pack_h2(sc[mt][2], sc[mt][3]);
+      const float2 f0 = __half22float2(u32_as_h2(h0)), f1 = __half22float2(u32_as_h2(h1));
+      const uint32_t bh0 = movmatrix_trans(h0), bh1 = movmatrix_trans(h1);
+      const uint32_t bl0 = movmatrix_trans(pack_h2(sc[mt][0] - f0.x, sc[mt][1] - f0.y));
+      const uint32_t bl1 = movmatrix_trans(pack_h2(sc[mt][2] - f1.x, sc[mt][3] - f1.y));
+      const uint32_t kBias = 0x64806480u;  // float16 1152 in both halves
+#pragma unroll
+      for (int G = 0; G < 4; ++G) {
+        const uint4 W = lds128(vcodes + mt * 2048 + G * 512 + lane * 16);
+        auto dq = [&](uint32_t w, uint32_t sel, uint32_t sc2) {
+          return hmul2u(h2_as_u32(__hsub2(u32_as_h2(prmt(w, K, sel)), u32_as_h2(kBias))), sc2);
+        };
+        const uint32_t a0 = dq(W.x, 0x4140, s01[G]), a1 = dq(W.x, 0x4342, s01[G]);
+        const uint32_t a2 = dq(W.z, 0x4140, s89[G]), a3 = dq(W.z, 0x4342, s89[G]);
+        mma16816(A.o[2 * G], a0, a1, a2, a3, bh0, bh1);
+        mma16816(A.o[2 * G], a0, a1, a2, a3, bl0, bl1);
+        const uint32_t c0 = dq(W.y, 0x4140, s01[G]), c1 = dq(W.y, 0x4342, s01[G]);
+        const uint32_t c2 = dq(W.w, 0x4140, s89[G]), c3 = dq(W.w, 0x4342, s89[G]);
+        mma16816(A.o[2 * G + 1], c0, c1, c2, c3, bh0, bh1);
+        mma16816(A.o[2 * G + 1], c0, c1, c2, c3, bl0, bl1);
+      }
+      continue;
+    }
+    const uint32_t kOne = 0x3C003C00u;
+    const uint32_t b0 = movmatrix_trans(pack_h2(sc[mt][0], sc[mt][1]));
+    const uint32_t b1 = movmatrix_trans(pack_h2(sc[mt][2], sc[mt][3]));
 #pragma unroll
     for (int G = 0; G < 4; ++G) {
       const uint32_t bg0 = hmul2u(b0, s01[G]), bg1 = hmul2u(b1, s89[G]);
       // Biased codes of this lane's A fragments for tiles 2G and 2G+1, token pairs interleaved.
       const uint4 W = lds128(vcodes + mt * 2048 + G * 512 + lane * 16);
-      const uint32_t K = 0x64646464u;
       mma16816(A.o[2 * G], prmt(W.x, K, 0x4140), prmt(W.x, K, 0x4342), prmt(W.z, K, 0x4140), prmt(W.z, K, 0x4342), bg0, bg1);
       mma16816(A.o[2 * G + 1], prmt(W.y, K, 0x4140), prmt(W.y, K, 0x4342), prmt(W.w, K, 0x4140), prmt(W.w, K, 0x4342), bg0, bg1);
       mma16816(A.ones[G], kOne, kOne, kOne, kOne, bg0, bg1);
@@ -474,6 +512,7 @@ __device__ __forceinline__ void load_q_frags(const AttnParams& P, int qh_base, i
 }
 
 // Write this warp's partial (m, l, o) for the heads < gc to a [gc][130] record.
+template <bool kExact>
 __device__ __forceinline__ void store_warp_partial(WarpAcc& A, float* rec, int gc, int lane) {
   const int g = lane >> 2, t = lane & 3;
   float l0 = A.l[0], l1 = A.l[1];
@@ -487,7 +526,7 @@ __device__ __forceinline__ void store_warp_partial(WarpAcc& A, float* rec, int g
   for (int md = 0; md < 8; ++md) {
     const int G = md >> 1;
     const int d = 32 * G + 4 * g + 2 * (md & 1);
-    const float c0 = 1152.f * A.ones[G][0], c1 = 1152.f * A.ones[G][1];
+    const float c0 = kExact ? 0.f : 1152.f * A.ones[G][0], c1 = kExact ? 0.f : 1152.f * A.ones[G][1];
     if (h0 < gc) {
       rec[h0 * TP_PARTIAL_FLOATS + 2 + d] = A.o[md][0] - c0;
       rec[h0 * TP_PARTIAL_FLOATS + 3 + d] = A.o[md][2] - c0;
@@ -587,6 +626,7 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity) { retu
 template <int kMode>
 __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __grid_constant__ AttnParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
+  constexpr bool kExactPV = (TP_EXACT_PV >> kMode) & 1;
   __shared__ tp_state s_pre;  // cache state as read before the wait, one read for the CTA
   __shared__ float s_wt[2][kMaxHeads][kConsumers + 1];  // merge weights, then the maximum
   float2* lut = reinterpret_cast<float2*>(smem + P.smem_lut_off);
@@ -730,7 +770,7 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
     for (int k = warp; k < n; k += kConsumers) {
       const int3 u = unit_ref(pt, k);
       if (u.x != cur) {
-        if (cur == 0) store_warp_partial(A, merge + warp * rec_stride, gc, lane);
+        if (cur == 0) store_warp_partial<kExactPV>(A, merge + warp * rec_stride, gc, lane);
         else if (u.x == 1) store_empty_partial(merge + warp * rec_stride, gmax, lane);
         cur = u.x;
         const int vh = vh_first + cur, chunk = vh % P.nqc;
@@ -775,13 +815,13 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
     }
     // Segment 0 partials go to the merge region now; segment 1 partials to this warp's ring
     // stage once every consumer is done with the ring (all issued copies have landed).
-    if (cur == 0) store_warp_partial(A, merge + warp * rec_stride, gc, lane);
+    if (cur == 0) store_warp_partial<kExactPV>(A, merge + warp * rec_stride, gc, lane);
     else if (cur == -1) store_empty_partial(merge + warp * rec_stride, gmax, lane);
     if (timed_out && lane == 0) atomicExch(P.ws_error, 1);  // word 0: 1 after a stage-wait timeout
     asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers * 32) : "memory");
     if (nseg > 1) {
       float* rec1 = reinterpret_cast<float*>(ring + warp * P.stage_bytes);
-      if (cur == 1) store_warp_partial(A, rec1, gc, lane);
+      if (cur == 1) store_warp_partial<kExactPV>(A, rec1, gc, lane);
       else store_empty_partial(rec1, gmax, lane);
     }
   }
