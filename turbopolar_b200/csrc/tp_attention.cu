@@ -1127,50 +1127,88 @@ __device__ __forceinline__ bool exchange_merge(const AttnParams& P, int qh, int 
     }
   }
   __shared__ int s_ok;
+  __shared__ float s_x[3][kD];
   if (tid == 0) s_ok = 1;
   __syncthreads();
-  if (tid < kD) {
-    // Each thread reads the (m, l, o[tid]) words of every rank's record once they carry this
-    // epoch (m first: the merge needs the maximum before the weights).
-    const uint64_t* base = reinterpret_cast<const uint64_t*>(P.xbuf[P.xrank]) + (slot * hq + qh) * kExchWords;
-    float m[TP_MAX_RANKS], l[TP_MAX_RANKS], o[TP_MAX_RANKS];
-    bool ok = true;
-    const long long t0 = clock64();
+  // Threads t and t + 128 take channel t & 127, the first the even ranks and the second the odd
+  // ones.  A pass loads the (m, l, o[channel]) words of two ranks still missing before it checks
+  // either, so once the records are here the wait costs one memory round trip for up to 4 ranks
+  // and two for 8, not one per rank.
+  constexpr int kPer = TP_MAX_RANKS / 2;
+  const int d = tid & (kD - 1), par = tid >> 7;
+  const uint64_t* base = reinterpret_cast<const uint64_t*>(P.xbuf[P.xrank]) + (slot * hq + qh) * kExchWords;
+  float m[kPer], l[kPer], o[kPer];
 #pragma unroll
-    for (int r = 0; r < TP_MAX_RANKS; ++r) {
-      m[r] = -INFINITY;
-      l[r] = o[r] = 0.f;
-      if (r < W && ok) {
-        const uint64_t* rec = base + size_t(r) * hq * kExchWords;
-        uint64_t wm, wl, wo;
-        while (true) {
-          wm = ld_word_sys(rec);
-          wl = ld_word_sys(rec + 1);
-          wo = ld_word_sys(rec + 2 + tid);
-          if (uint32_t(wm >> 32) == ep && uint32_t(wl >> 32) == ep && uint32_t(wo >> 32) == ep) break;
-          if (clock64() - t0 > (1ll << 31)) { ok = false; break; }
-        }
-        m[r] = __uint_as_float(uint32_t(wm));
-        l[r] = __uint_as_float(uint32_t(wl));
-        o[r] = __uint_as_float(uint32_t(wo));
+  for (int j = 0; j < kPer; ++j) {
+    m[j] = -INFINITY;
+    l[j] = o[j] = 0.f;
+  }
+  bool ok = true;
+  const long long t0 = clock64();
+#pragma unroll
+  for (int jg = 0; jg < kPer; jg += 2) {
+    bool got0 = 2 * jg + par >= W, got1 = 2 * (jg + 1) + par >= W;  // ranks beyond the world: nothing
+    while (ok && !(got0 && got1)) {
+      uint64_t w0[3], w1[3];
+      if (!got0) {
+        const uint64_t* rec = base + size_t(2 * jg + par) * hq * kExchWords;
+        w0[0] = ld_word_sys(rec);
+        w0[1] = ld_word_sys(rec + 1);
+        w0[2] = ld_word_sys(rec + 2 + d);
       }
-    }
-    if (!ok) s_ok = 0;
-    float Mx = -INFINITY;
-#pragma unroll
-    for (int r = 0; r < TP_MAX_RANKS; ++r) Mx = fmaxf(Mx, m[r]);
-    float Lx = 0.f, Ox = 0.f;
-    if (ok && Mx != -INFINITY) {
-#pragma unroll
-      for (int r = 0; r < TP_MAX_RANKS; ++r) {
-        const float w = (m[r] == -INFINITY) ? 0.f : exp2_approx(m[r] - Mx);
-        Lx = fmaf(l[r], w, Lx);
-        Ox = fmaf(o[r], w, Ox);
+      if (!got1) {
+        const uint64_t* rec = base + size_t(2 * (jg + 1) + par) * hq * kExchWords;
+        w1[0] = ld_word_sys(rec);
+        w1[1] = ld_word_sys(rec + 1);
+        w1[2] = ld_word_sys(rec + 2 + d);
       }
+      if (!got0 && uint32_t(w0[0] >> 32) == ep && uint32_t(w0[1] >> 32) == ep && uint32_t(w0[2] >> 32) == ep) {
+        got0 = true;
+        m[jg] = __uint_as_float(uint32_t(w0[0]));
+        l[jg] = __uint_as_float(uint32_t(w0[1]));
+        o[jg] = __uint_as_float(uint32_t(w0[2]));
+      }
+      if (!got1 && uint32_t(w1[0] >> 32) == ep && uint32_t(w1[1] >> 32) == ep && uint32_t(w1[2] >> 32) == ep) {
+        got1 = true;
+        m[jg + 1] = __uint_as_float(uint32_t(w1[0]));
+        l[jg + 1] = __uint_as_float(uint32_t(w1[1]));
+        o[jg + 1] = __uint_as_float(uint32_t(w1[2]));
+      }
+      if (clock64() - t0 > (1ll << 31)) ok = false;
     }
-    M = Mx;
-    L = Lx;
-    O = Ox;
+  }
+  if (!ok) s_ok = 0;
+  float Mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) Mx = fmaxf(Mx, m[j]);
+  float Lx = 0.f, Ox = 0.f;
+  if (Mx != -INFINITY) {
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const float w = (m[j] == -INFINITY) ? 0.f : exp2_approx(m[j] - Mx);
+      Lx = fmaf(l[j], w, Lx);
+      Ox = fmaf(o[j], w, Ox);
+    }
+  }
+  if (par) {
+    s_x[0][d] = Mx;
+    s_x[1][d] = Lx;
+    s_x[2][d] = Ox;
+  }
+  __syncthreads();
+  if (!par) {
+    const float m1 = s_x[0][d], l1 = s_x[1][d], o1 = s_x[2][d];
+    const float Mt = fmaxf(Mx, m1);
+    float Lt = 0.f, Ot = 0.f;
+    if (s_ok && Mt != -INFINITY) {
+      const float a0 = (Mx == -INFINITY) ? 0.f : exp2_approx(Mx - Mt);
+      const float a1 = (m1 == -INFINITY) ? 0.f : exp2_approx(m1 - Mt);
+      Lt = Lx * a0 + l1 * a1;
+      Ot = Ox * a0 + o1 * a1;
+    }
+    M = Mt;
+    L = Lt;
+    O = Ot;
   }
   __syncthreads();
   return s_ok != 0;
