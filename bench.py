@@ -558,6 +558,8 @@ def run_gpu(args):
 
     from turbopolar_b200 import TurboPolarConfig, build, graph
     build.build()
+    library = {"path": os.path.relpath(build.LIB, ROOT), "source_sha16": build.last_build["source_sha16"],
+               "compiled_in_this_run": build.last_build["compiled"]}
     cfg = TurboPolarConfig(num_q_heads=HQ, num_kv_heads=HKV)
     ctx = _total_ctx(args, world)
     layers = _make_layers(cfg, ctx, world, rank, dev, args.steps + args.warmup + 2, seed0=1000)
@@ -655,7 +657,7 @@ def run_gpu(args):
             # cross-GPU merge runs inside the split combine).
             "gpu_launches": args.steps * LAYERS * 2,
             "roofline": roof, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary(),
-            "device_errors": err, **extra,
+            "device_errors": err, "library": library, **extra,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
