@@ -137,3 +137,15 @@ def test_append_rejects_without_gpu_work():
     assert rt.get_io_telemetry() == {}
     with pytest.raises(RuntimeError, match="no blocks"):
         rt.attention(torch.zeros(1, 4, 128))
+
+
+def test_build_is_keyed_by_a_hash_of_sources_and_flags(lib):
+    """A second build() with the same sources and flags reuses the library; other flags change
+    the hash, so a library built with them is not taken for the product build."""
+    from turbopolar_b200 import build
+    build.build()
+    assert build.last_build["compiled"] is False
+    assert build.last_build["source_sha16"] == build.source_hash()
+    with open(build.STAMP) as f:
+        assert f.read().strip() == build.source_hash()
+    assert build.source_hash(["-DTP_QK_CUDA_CORES=1"]) != build.source_hash()
