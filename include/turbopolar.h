@@ -173,6 +173,21 @@ int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state 
                         int32_t num_q_heads, float scale, void* out, float* partial_out,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Fused decode attention over compressed keys and dense float16 values.  Replaces
+ * MetalKernelBridge.execute_online_attention_dense_v (rfsn_v11/kernels/turbo_polar/
+ * metal.py:587-649, kernel tqpolar_online_attention.metal:10-195; numeric target its CPU
+ * fallback, metal.py:267-291): the keys of pool pages [0, state.n_pages) (their value codes
+ * are not read), the values v[h][t][:] of KV head h and token t = 64 * page + row, heads
+ * v_head_stride elements apart (a multiple of 8, >= 128 * v_tokens; v 16-byte aligned), tokens
+ * t >= state.seq_len masked.  state.tail_len and state.first_page must be 0 and
+ * 1 <= seq_len <= min(64 * n_pages, v_tokens); values past v_tokens read as zero.  Other
+ * arguments, the workspace and the output as tp_decode_attention. */
+int tp_decode_attention_dense_v(const tp_page_pool* pool, tp_state state, const void* v,
+                                int64_t v_head_stride, int64_t v_tokens, const void* q,
+                                int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
+                                float* partial_out, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
 /* One decode step in one call: append one token per KV head, then attend over everything
  * including it.  Replaces TurboPolarFastCache.decode_attention
  * (benchmarks/turbopolar_fast_attention.py:106-188), i.e. TurboPolarKVCacheRuntime.append

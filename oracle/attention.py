@@ -77,6 +77,16 @@ def attention_dense_tail(q, pages: dict | None, fmt: dict, tail_k, tail_v, actua
     return attention(q, np.concatenate(parts_k, axis=1), np.concatenate(parts_v, axis=1), actual_seq_len, scale)
 
 
+def attention_dense_v(q, pages: dict, fmt: dict, v_dense, actual_seq_len: int, scale: float) -> np.ndarray:
+    """Compressed keys with dense values (``execute_online_attention_dense_v``'s fallback,
+    ``metal.py:587-603`` into ``_cpu_online_attention``, ``:267-291``); float64 ``(H_q,128)``.
+
+    ``v_dense`` is ``(H_kv, S*64, 128)``; the value codes in ``pages`` are not used.
+    """
+    k, _ = decode_pages(pages, fmt)
+    return attention(q, k.astype(np.float64), np.asarray(v_dense, np.float64), actual_seq_len, scale)
+
+
 def partial(q, k, v, scale: float) -> np.ndarray:
     """Unnormalised softmax partial of ``q (H_q,128)`` over one token range ``k, v (H_kv,T,128)``:
     ``[H_q, 130]`` records ``(m, l, o[128])`` with ``m`` the maximum score in base-2 units,

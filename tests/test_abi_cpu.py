@@ -77,6 +77,35 @@ def test_error_statuses_map_to_reference_exceptions(lib):
         _lib.check(lib.tp_decode_pages(ctypes.byref(pool2), 0, 0, None, None, None))
 
 
+def test_dense_v_rejects_bad_arguments_before_any_launch(lib):
+    """tp_decode_attention_dense_v's argument checks (pages only, the token range, the value
+    array's alignment and strides), each a ValueError before any CUDA call."""
+    from turbopolar_b200 import _lib
+    f = _lib.Format(4, 4, 64, 0)
+    pool = _lib.PagePool(ctypes.c_void_p(1 << 20), None, 2, 4, f)
+    v = ctypes.c_void_p(1 << 24)
+
+    def call(state, v=v, stride=4 * 64 * 128, tokens=4 * 64):
+        return lib.tp_decode_attention_dense_v(ctypes.byref(pool), state, v, stride, tokens, ctypes.c_void_p(16), 0,
+                                               4, 0.1, ctypes.c_void_p(16), None, None, 0, None)
+
+    cases = [
+        ((2, 5, 133, 0), {}, "pages only"),
+        ((2, 0, 100, 1), {}, "pages only"),
+        ((0, 0, 1, 0), {}, "n_pages must be in"),
+        ((5, 0, 1, 0), {}, "n_pages must be in"),
+        ((2, 0, 129, 0), {}, "seq_len must be in"),
+        ((2, 0, 0, 0), {}, "seq_len must be in"),
+        ((2, 0, 100, 0), dict(v=ctypes.c_void_p((1 << 24) + 8)), "16-byte aligned"),
+        ((2, 0, 100, 0), dict(tokens=99), "v_tokens"),
+        ((2, 0, 100, 0), dict(stride=4 * 64 * 128 + 4), "v_head_stride"),
+        ((2, 0, 100, 0), dict(stride=64 * 128), "v_head_stride"),
+    ]
+    for state, kw, pattern in cases:
+        with pytest.raises(ValueError, match=pattern):  # the message is read right after the call
+            _lib.check(call(_lib.State(*state), **kw))
+
+
 def test_workspace_size(lib):
     n = lib.tp_decode_attention_workspace_size(8, 32)
     assert n > 0 and n % 256 == 0

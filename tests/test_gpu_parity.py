@@ -343,8 +343,8 @@ def test_errors():
         rt.attention(torch.zeros((1, 8, 2, 128), dtype=torch.float16, device=DEV))
     with pytest.raises(ValueError, match="GQA ratio"):
         rt.attention(torch.zeros((1, 6, 128), dtype=torch.float16, device=DEV))
-    with pytest.raises(NotImplementedError):
-        CudaKernelBridge().execute_online_attention_dense_v()
+    with pytest.raises(NotImplementedError, match="QJL"):
+        CudaKernelBridge().execute_online_attention_dense_v(None, None, None, None, None, cfg, 1, use_qjl=True)
     rt.reset()
     rt.append(torch.zeros((2, 4, 1, 128), dtype=torch.float16, device=DEV), torch.zeros((2, 4, 1, 128), dtype=torch.float16, device=DEV))
     assert rt._batch_size == 2

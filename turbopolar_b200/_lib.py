@@ -20,7 +20,7 @@ STATE_WORDS = 6
 
 EXPORTED = (
     "tp_row_bytes", "tp_unit_bytes", "tp_encode_pages", "tp_append", "tp_decode_attention_workspace_size",
-    "tp_decode_attention", "tp_decode_step", "tp_decode_attention_noalloc", "tp_noalloc_error", "tp_combine_partials", "tp_fused_scores", "tp_decode_pages",
+    "tp_decode_attention", "tp_decode_attention_dense_v", "tp_decode_step", "tp_decode_attention_noalloc", "tp_noalloc_error", "tp_combine_partials", "tp_fused_scores", "tp_decode_pages",
     "tp_export_pages", "tp_import_pages", "tp_last_error", "tp_version",
     "tp_exchange_bytes", "tp_ipc_alloc", "tp_ipc_open", "tp_ipc_close", "tp_ipc_free",
     "tp_decode_attention_sharded", "tp_decode_step_sharded",
@@ -85,6 +85,8 @@ def _declare(lib):
         "tp_decode_attention_workspace_size": (SZ, [I32, I32]),
         "tp_decode_attention": (ctypes.c_int, [ctypes.POINTER(PagePool), ctypes.POINTER(Tail), State, P, P, I32, I32,
                                                F, P, P, P, SZ, P]),
+        "tp_decode_attention_dense_v": (ctypes.c_int, [ctypes.POINTER(PagePool), State, P, I64, I64, P, I32, I32, F,
+                                                       P, P, P, SZ, P]),
         "tp_decode_step": (ctypes.c_int, [ctypes.POINTER(PagePool), ctypes.POINTER(Tail), P, P, P, I32, I64, P, I32,
                                           I32, F, P, P, P, SZ, P]),
         "tp_decode_attention_noalloc": (ctypes.c_int, [ctypes.POINTER(PagePool), ctypes.POINTER(Tail), State, P, P,

@@ -115,10 +115,34 @@ class CudaKernelBridge:
         out = self._attention(q, block, quant_v, tail_k, tail_v, config, actual_seq_len)
         return out, self._trace("tp_decode_attention_dense_tail", q, block, actual_seq_len, tail=tail_k)
 
-    def execute_online_attention_dense_v(self, *args, **kwargs):
-        """Dense-V debug storage is rejected by the configuration contract
-        (``turbo_polar_config.py:48-49``); its kernel (``metal.py:587-649``) is not provided."""
-        raise NotImplementedError("TurboPolar only supports storage_mode='kv_quant' in this release")
+    def execute_online_attention_dense_v(self, q, block, v_dense, qjl_payload, q_proj_signs, config,
+                                         actual_seq_len: int, use_qjl: bool = False) -> Tuple[torch.Tensor, Dict[str, Any]]:
+        """Compressed keys with dense values (``metal.py:587-649``): ``v_dense`` is
+        ``(B, H_kv, S, 64, 128)`` or ``(B, H_kv, S*64, 128)``, read as float16 as the reference's
+        kernel reads it (``tqpolar_online_attention.metal:16``).  Tokens ``>= actual_seq_len``
+        are masked; ``actual_seq_len`` beyond ``S*64`` attends to every token.  The configuration
+        contract still rejects dense-V storage (``turbo_polar_config.py:48-49``): this entry point
+        serves callers that hold the values themselves, as the reference's debug kernel does."""
+        self._reject_qjl(use_qjl)
+        pool, B, H, S = pool_of_block(block)
+        q = q.contiguous()
+        Hq = q.shape[1]
+        heads = B * H
+        tokens = S * PAGE
+        if v_dense.numel() != heads * tokens * 128:
+            raise ValueError(f"v_dense must hold (B, H_kv, S*64, 128) = ({B}, {H}, {tokens}, 128) values")
+        if int(actual_seq_len) < 1:
+            raise ValueError("actual_seq_len must be at least 1")
+        v = v_dense.reshape(heads, tokens, 128).to(torch.float16).contiguous()
+        out = torch.empty((B, Hq, 128), dtype=torch.float16, device=q.device)
+        ws = self._workspace(q.device, heads, B * Hq)
+        _lib.check(_lib.lib().tp_decode_attention_dense_v(
+            ctypes.byref(pool.struct()), _lib.State(S, 0, min(int(actual_seq_len), tokens), 0), v.data_ptr(),
+            tokens * 128, tokens, q.data_ptr(), _qcode(q), B * Hq, float(config.attention_scale), out.data_ptr(), None,
+            ws.data_ptr(), ws.numel(), _stream(q.device)))
+        tr = self._trace("tp_decode_attention_dense_v", q, block, actual_seq_len, tail=None)
+        tr["quant_v_used"] = False
+        return out, tr
 
     @staticmethod
     def _trace(name, q, block, actual_seq_len, tail) -> Dict[str, Any]:

@@ -32,12 +32,21 @@
 // decode step, appends the new token) while the page pass runs, then waits for it to complete
 // and merges the partials of each query head into the fp16 output (sharded: with the other
 // ranks' records, exchanged over NVLink in the same launch).
+//
+// Dense-V variant (tp_decode_attention_dense_v; the reference's tqpolar_online_attention_dense_v,
+// tqpolar_online_attention.metal:10-195): compressed keys, float16 values in a separate
+// [head][token][128] array.  A stage holds the unit's radii and angle codes (two bulk copies)
+// and its 32 value rows (two TMA tensor copies of 32 tokens x 64 channels, 128-byte swizzle), and
+// P.V multiplies the value rows as they are, with P as float16 hi + lo parts.
 #include <cfloat>
 #include <cstring>
 #include <cmath>
 #include <functional>
 #include <mutex>
 #include <thread>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include "tp_codec.cuh"
 #include "tp_overlap.h"
@@ -123,6 +132,13 @@ struct AttnParams {
   // (uint2 (cos_hi, sin_hi), (cos_lo, sin_lo)) in the first 16 slots, or the adapter path's 256
   // deep entries as float2.  The general path builds its tables on the device.
   float2 cs[kLutEntries];
+  // Dense-V variant: a stage holds the unit's radii at 0 (k_radii_bytes), its angle codes at
+  // off_codes (k_code_bytes, copied from unit offset k_src_codes) and its value rows at
+  // off_vdense (1024-byte aligned: two 4 KB boxes, channels 0-63 then 64-127, each token row
+  // 128 bytes with 16-byte chunk c stored at c ^ (row & 7)); vmap is the tensor map of the value
+  // array {128 channels, tokens, KV heads}.
+  int k_radii_bytes, k_code_bytes, k_src_codes, off_vdense;
+  CUtensorMap vmap;
 };
 
 // Work partition: the U units (half pages, head-major, uph per head) are cut into C = min(U,
@@ -338,7 +354,13 @@ enum { kModeGeneral = 0, kModeFast = 1, kModeAdapter = 2 };
 __device__ __forceinline__ int qcc_off(int j) { return j * 8 + (j >> 4) * 4; }
 constexpr int kQccFloats = 528;
 
-template <int kMode>
+// Formats whose P.V is exact: the TP_EXACT_PV key formats, and every format with dense values.
+template <int kMode, bool kDenseV>
+__host__ __device__ constexpr bool exact_pv() {
+  return kDenseV || ((TP_EXACT_PV >> kMode) & 1);
+}
+
+template <int kMode, bool kDenseV>
 __device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, const AttnParams& P, const float2* lut,
                                              const float2* tab, const uint32_t (&qf)[16], float radius_scale,
                                              int valid_tokens, int lane
@@ -407,8 +429,42 @@ __device__ __forceinline__ void process_half(WarpAcc& A, const uint8_t* stage, c
       if (16 * mt + g + 8 >= valid_tokens) sc[mt][2] = sc[mt][3] = -INFINITY;
     }
   }
-  constexpr bool kExact = (TP_EXACT_PV >> kMode) & 1;
+  constexpr bool kExact = exact_pv<kMode, kDenseV>();
   softmax_update<2, !kExact>(A, sc, P.scale_log2);
+  if (kDenseV) {
+    // Tile 2G (2G+1) rows g, g + 8 are channels d0, d0 + 1 (d0 + 2, d0 + 3), d0 = 32G + 4g, as
+    // the code path's tiles (store_warp_partial).  Lane (g, t) reads 8 bytes (channels d0 ..
+    // d0 + 3) of tokens 2t, 2t + 1, 2t + 8, 2t + 9 of the 16-token tile: in box G / 2 at chunk
+    // 4(G & 1) + g / 2, byte 8(g & 1); with the chunk swizzled by the token row, the 16 lanes of
+    // a half warp read 16 different 8-byte bank pairs.  One byte permute then pairs the two
+    // tokens of a fragment register.
+    const uint8_t* vd = stage + P.off_vdense;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const uint32_t h0 = pack_h2(sc[mt][0], sc[mt][1]), h1 = pack_h2(sc[mt][2], sc[mt][3]);
+      const float2 f0 = __half22float2(u32_as_h2(h0)), f1 = __half22float2(u32_as_h2(h1));
+      const uint32_t bh0 = movmatrix_trans(h0), bh1 = movmatrix_trans(h1);
+      const uint32_t bl0 = movmatrix_trans(pack_h2(sc[mt][0] - f0.x, sc[mt][1] - f0.y));
+      const uint32_t bl1 = movmatrix_trans(pack_h2(sc[mt][2] - f1.x, sc[mt][3] - f1.y));
+      const int r0 = 16 * mt + 2 * t;
+#pragma unroll
+      for (int G = 0; G < 4; ++G) {
+        const uint8_t* box = vd + (G >> 1) * 4096 + 8 * (g & 1);
+        const int ch = 4 * (G & 1) + (g >> 1);
+        auto row = [&](int r) { return lds64(box + r * 128 + ((ch ^ (r & 7)) << 4)); };
+        const uint2 x0 = row(r0), x1 = row(r0 + 1), x8 = row(r0 + 8), x9 = row(r0 + 9);
+        const uint32_t a0 = prmt(x0.x, x1.x, 0x5410), a1 = prmt(x0.x, x1.x, 0x7632);
+        const uint32_t a2 = prmt(x8.x, x9.x, 0x5410), a3 = prmt(x8.x, x9.x, 0x7632);
+        mma16816(A.o[2 * G], a0, a1, a2, a3, bh0, bh1);
+        mma16816(A.o[2 * G], a0, a1, a2, a3, bl0, bl1);
+        const uint32_t c0 = prmt(x0.y, x1.y, 0x5410), c1 = prmt(x0.y, x1.y, 0x7632);
+        const uint32_t c2 = prmt(x8.y, x9.y, 0x5410), c3 = prmt(x8.y, x9.y, 0x7632);
+        mma16816(A.o[2 * G + 1], c0, c1, c2, c3, bh0, bh1);
+        mma16816(A.o[2 * G + 1], c0, c1, c2, c3, bl0, bl1);
+      }
+    }
+    return;
+  }
   const uint8_t* vcodes = stage + P.off_vcodes;
   const uint8_t* vscales = stage + P.off_vscales;
   const uint32_t K = 0x64646464u;  // float16 0x64xx = 1024 + xx: a byte permute makes code + 1152
@@ -474,6 +530,26 @@ __device__ __forceinline__ void issue_half(uint8_t* stage, uint64_t* bar, const 
   fence_proxy_async_smem();
   mbar_arrive_expect_tx(bar, bytes);
   if (bytes) bulk_g2s_hint(stage + off, P.pages + unit * P.unit_bytes + off, bytes, bar, pol);
+}
+
+// Dense-V variant: the unit's radii and angle codes (bulk copies) and the 32 value rows of its
+// tokens (page * 64 + half * 32 of KV head kvh in the value array; two TMA boxes), all by part
+// 0; the other parts only arrive.
+__device__ __forceinline__ void issue_half_dense_v(uint8_t* stage, uint64_t* bar, const AttnParams& P, int kvh,
+                                                   int page, int half, int part, uint64_t pol) {
+  if (part != 0) {
+    mbar_arrive(bar);
+    return;
+  }
+  const int64_t unit = (int64_t(kvh) * P.page_capacity + page) * 2 + half;
+  const uint8_t* src = P.pages + unit * P.unit_bytes;
+  const int tok = page * kPage + half * kHalf;
+  fence_proxy_async_smem();
+  mbar_arrive_expect_tx(bar, uint32_t(P.k_radii_bytes + P.k_code_bytes + 2 * kHalf * 64 * 2));
+  bulk_g2s_hint(stage, src, uint32_t(P.k_radii_bytes), bar, pol);
+  bulk_g2s_hint(stage + P.off_codes, src + P.k_src_codes, uint32_t(P.k_code_bytes), bar, pol);
+  tma_load_3d(stage + P.off_vdense, &P.vmap, 0, tok, kvh, bar, pol);
+  tma_load_3d(stage + P.off_vdense + 4096, &P.vmap, 64, tok, kvh, bar, pol);
 }
 
 // Bounded wait for phase `parity` of a stage barrier (about a second); false on timeout.
@@ -623,10 +699,10 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity) { retu
 #else
 #define TP_PAGE_PASS_REGS 192
 #endif
-template <int kMode>
+template <int kMode, bool kDenseV>
 __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __grid_constant__ AttnParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
-  constexpr bool kExactPV = (TP_EXACT_PV >> kMode) & 1;
+  constexpr bool kExactPV = exact_pv<kMode, kDenseV>();
   __shared__ tp_state s_pre;  // cache state as read before the wait, one read for the CTA
   __shared__ float s_wt[2][kMaxHeads][kConsumers + 1];  // merge weights, then the maximum
   float2* lut = reinterpret_cast<float2*>(smem + P.smem_lut_off);
@@ -634,6 +710,9 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.smem_bar_off);
   uint64_t* empty = full + kMaxStages;
   uint8_t* ring = smem + P.smem_stage_off;
+  // Dense values: the swizzled TMA boxes need 1024-byte aligned shared addresses (the host
+  // reserves 1024 bytes for this).
+  if (kDenseV) ring += (1024u - (smem_u32(ring) & 1023u)) & 1023u;
   float* stage_scale = reinterpret_cast<float*>(smem + P.smem_scale_off);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int R = P.n_stages, S = R / kConsumers;
@@ -645,6 +724,7 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
   const int pcons = pw / kCopySplit, ppart = pw % kCopySplit;  // the consumer and part it serves
   const int c = blockIdx.x;
   const uint64_t pol = l2_evict_first_policy();
+  if (kDenseV && issuer && pw == 0) prefetch_tmap(&P.vmap);
 
   // Before the previous kernel in the stream has completed (this grid is its programmatic
   // dependent): the code tables, the ring barriers and the first copies, none of which
@@ -696,7 +776,8 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
     // stage's full barrier, which releases it to the consumer.
     if (P.int8_radii && ppart == 0)
       stage_scale[slot] = __half2float(P.radii_scales[int64_t(kvh) * P.page_capacity + u.y]);
-    issue_half(ring + slot * P.stage_bytes, &full[slot], P, kvh, u.y, u.z, ppart, pol);
+    if (kDenseV) issue_half_dense_v(ring + slot * P.stage_bytes, &full[slot], P, kvh, u.y, u.z, ppart, pol);
+    else issue_half(ring + slot * P.stage_bytes, &full[slot], P, kvh, u.y, u.z, ppart, pol);
   };
   // Units [j0, j1) of the consumer this lane serves.
   auto produce_range = [&](int j0, int j1) {
@@ -801,7 +882,7 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
         const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, kHalf));
         // The adapter path takes the radius scale in base-2 units.
         const float rs = P.int8_radii ? stage_scale[slot] * (kMode == kModeAdapter ? 1.4426950408889634f : 1.f) : 0.f;
-        process_half<kMode>(A, ring + slot * P.stage_bytes, P, lut, tab, qf, rs, vt, lane
+        process_half<kMode, kDenseV>(A, ring + slot * P.stage_bytes, P, lut, tab, qf, rs, vt, lane
 #if TP_QK_CUDA_CORES
                             , qcc
 #endif
@@ -1415,11 +1496,12 @@ __global__ void combine_kernel(const float* partials, int n_parts, int num_q_hea
 // how much of it each page-pass variant has been allowed so far (cudaFuncSetAttribute acts on
 // the current device).
 constexpr int kModes = 3;
+constexpr int kVariants = 2 * kModes;  // key format x (value codes, dense values)
 constexpr int kMaxDevices = 64;
 struct DeviceCfg {
   int sms = 0;
-  int ring_budget[kModes] = {};
-  int attr_bytes[kModes] = {};
+  int ring_budget[kVariants] = {};
+  int attr_bytes[kVariants] = {};
 };
 static std::mutex g_cfg_mutex;
 static DeviceCfg g_cfg[kMaxDevices];
@@ -1442,13 +1524,13 @@ static int num_sms() {
   return cfg.sms;
 }
 
-// Dynamic shared memory the page pass (variant `mode`, kernel `page_pass`) may use: the opt-in
+// Dynamic shared memory the page pass (variant `variant`, kernel `page_pass`) may use: the opt-in
 // per-block limit and, when the registers allow a split-combine CTA beside a page-pass CTA on
 // one SM (so it starts, and finishes the dense tail, while the page pass runs), no more than
 // leaves room for it.
-static int ring_budget(int mode, const void* page_pass) {
+static int ring_budget(int variant, const void* page_pass) {
   std::lock_guard<std::mutex> lock(g_cfg_mutex);
-  int& budget = device_cfg().ring_budget[mode];
+  int& budget = device_cfg().ring_budget[variant];
   if (budget == 0) {
     int dev = 0, per_sm = 233472, per_block = 232448, reserved = 1024, regs = 65536;
     cudaGetDevice(&dev);
@@ -1468,12 +1550,12 @@ static int ring_budget(int mode, const void* page_pass) {
   return budget;
 }
 
-// Let the page pass (variant `mode`) use `smem` bytes of dynamic shared memory on the current
+// Let the page pass (variant `variant`) use `smem` bytes of dynamic shared memory on the current
 // device, and all of the unified L1/shared array as shared memory for it and the split
 // combine, so the split-combine CTAs fit beside a page-pass CTA.
-static cudaError_t reserve_smem(int mode, const void* page_pass, int smem) {
+static cudaError_t reserve_smem(int variant, const void* page_pass, int smem) {
   std::lock_guard<std::mutex> lock(g_cfg_mutex);
-  int& have = device_cfg().attr_bytes[mode];
+  int& have = device_cfg().attr_bytes[variant];
   if (smem <= have) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(page_pass, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(page_pass, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
@@ -1539,6 +1621,61 @@ static StreamKey stream_key(cudaStream_t s) {
   return k;
 }
 
+// The page-pass kernels: one per key format, with value codes or dense values.
+template <int kMode, bool kDenseV>
+static cudaError_t launch_page_pass(const cudaLaunchConfig_t* c, const AttnParams& P) {
+  return cudaLaunchKernelEx(c, decode_attention_kernel<kMode, kDenseV>, P);
+}
+struct PagePass {
+  const void* fn;
+  cudaError_t (*launch)(const cudaLaunchConfig_t*, const AttnParams&);
+};
+template <int kMode, bool kDenseV>
+static PagePass page_pass_of() {
+  return {reinterpret_cast<const void*>(decode_attention_kernel<kMode, kDenseV>), launch_page_pass<kMode, kDenseV>};
+}
+static PagePass page_pass(int mode, bool dense_v) {
+  if (dense_v)
+    return mode == kModeFast ? page_pass_of<kModeFast, true>()
+           : mode == kModeAdapter ? page_pass_of<kModeAdapter, true>() : page_pass_of<kModeGeneral, true>();
+  return mode == kModeFast ? page_pass_of<kModeFast, false>()
+         : mode == kModeAdapter ? page_pass_of<kModeAdapter, false>() : page_pass_of<kModeGeneral, false>();
+}
+
+// cuTensorMapEncodeTiled from the driver (resolved once; NULL when the driver lacks it).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+// Tensor map of a float16 value array [heads][tokens][128] (head_stride elements between heads):
+// boxes of 64 channels x 32 tokens x 1 head, 128-byte swizzle, zero fill outside the array.
+static int encode_value_map(CUtensorMap* m, const void* v, int64_t tokens, int heads, int64_t head_stride) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(TP_ERR_CUDA, "tp_decode_attention_dense_v: the driver has no cuTensorMapEncodeTiled");
+  cuuint64_t dims[3] = {cuuint64_t(kD), cuuint64_t(tokens), cuuint64_t(heads)};
+  cuuint64_t strides[2] = {cuuint64_t(kD * 2), cuuint64_t(head_stride * 2)};
+  cuuint32_t box[3] = {64, cuuint32_t(kHalf), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(v), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TP_ERR_INVALID, "tp_decode_attention_dense_v: cannot describe the value array (CUresult " +
+                                    std::to_string(int(r)) + ")");
+  return TP_OK;
+}
+
 }  // namespace tp
 
 using namespace tp;
@@ -1559,10 +1696,17 @@ struct StepArgs {
   int64_t head_stride;
 };
 
+// The float16 value array of a dense-V call: [heads][tokens][128], heads head_stride elements apart.
+struct DenseV {
+  const void* v;
+  int64_t head_stride;
+  int64_t tokens;
+};
+
 static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state state, int32_t* d_state,
                          const void* q, int32_t q_dtype, int32_t num_q_heads, float scale, void* out,
                          float* partial_out, void* workspace, size_t workspace_bytes, void* stream,
-                         const StepArgs* step, const tp_exchange* x = nullptr) {
+                         const StepArgs* step, const tp_exchange* x = nullptr, const DenseV* dv = nullptr) {
   Layout L;
   int st = validate_pool(pool, &L);
   if (st != TP_OK) return st;
@@ -1639,12 +1783,25 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
     P.xrank = x->rank;
   }
   P.ws_partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
-  // Half-page stage: one unit copied linearly (radii | v codes | angle codes | v scales).
+  // Half-page stage: one unit copied linearly (radii | v codes | angle codes | v scales), or
+  // with dense values radii | angle codes | value rows (1024-byte aligned).
   auto up = [](int x, int a) { return (x + a - 1) / a * a; };
   P.off_vcodes = L.u_vcodes;
   P.off_codes = L.u_codes;
   P.off_vscales = L.u_vscales;
   P.stage_bytes = up(L.unit_bytes, 128);
+  P.k_radii_bytes = L.u_vcodes;
+  P.k_code_bytes = L.u_vscales - L.u_codes;
+  P.k_src_codes = L.u_codes;
+  P.off_vdense = 0;
+  std::memset(&P.vmap, 0, sizeof(P.vmap));
+  if (dv) {
+    P.off_codes = P.k_radii_bytes;
+    P.off_vdense = up(P.k_radii_bytes + P.k_code_bytes, 1024);
+    P.stage_bytes = P.off_vdense + 2 * kHalf * 64 * 2;
+    st = encode_value_map(&P.vmap, dv->v, dv->tokens, hkv, dv->head_stride);
+    if (st != TP_OK) return st;
+  }
   const int merge_bytes = kConsumers * P.gmax * TP_PARTIAL_FLOATS * int(sizeof(float));
   P.smem_bar_off = 0;                       // full and empty barrier per ring stage
   P.smem_lut_off = up(2 * kMaxStages * 8, 128);
@@ -1660,18 +1817,21 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
 
   fill_decoder_table(mode, P.cs);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const void* fn = mode == kModeFast      ? reinterpret_cast<const void*>(decode_attention_kernel<kModeFast>)
-                   : mode == kModeAdapter ? reinterpret_cast<const void*>(decode_attention_kernel<kModeAdapter>)
-                                          : reinterpret_cast<const void*>(decode_attention_kernel<kModeGeneral>);
+  const PagePass pass = page_pass(mode, dv != nullptr);
+  const void* fn = pass.fn;
+  const int variant = mode + (dv ? kModes : 0);
   // Ring stages: as many as fit while a split-combine CTA still fits beside the page-pass CTA
-  // on one SM (so it starts, and finishes the dense tail, while the page pass runs).
-  const int ring_bytes = ring_budget(mode, fn) - P.smem_stage_off;
+  // on one SM (so it starts, and finishes the dense tail, while the page pass runs); with dense
+  // values 1024 bytes go to aligning the ring, and one stage per compute warp is accepted (the
+  // stages are larger, and the seven warps' copies still keep the SM's share of HBM busy).
+  const int align_slack = dv ? 1024 : 0;
+  const int ring_bytes = ring_budget(variant, fn) - P.smem_stage_off - align_slack;
   P.n_stages = min(kMaxStages, ring_bytes / P.stage_bytes) / kConsumers * kConsumers;
-  if (P.n_stages < 2 * kConsumers)
+  if (P.n_stages < (dv ? 1 : 2) * kConsumers)
     return fail(TP_ERR_UNSUPPORTED, "tp_decode_attention: not enough shared memory for the page ring");
-  const int smem = P.smem_stage_off + P.n_stages * P.stage_bytes;
+  const int smem = P.smem_stage_off + align_slack + P.n_stages * P.stage_bytes;
   {
-    const cudaError_t e = reserve_smem(mode, fn, smem);
+    const cudaError_t e = reserve_smem(variant, fn, smem);
     if (e != cudaSuccess)
       return fail(TP_ERR_CUDA, std::string("tp_decode_attention: cannot reserve ") + std::to_string(smem) +
                                    " bytes of shared memory: " + cudaGetErrorString(e));
@@ -1704,6 +1864,10 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
       b.exchange = P.xbuf[P.xrank];
       b.exchange_bytes = x_epoch_off(P.xworld, num_q_heads) + 256;
     }
+    if (dv) {
+      b.values = dv->v;
+      b.values_bytes = size_t((hkv - 1) * dv->head_stride + dv->tokens * kD) * sizeof(__half);
+    }
     Spans reads, writes;
     call_spans(b, reads, writes);
     P.spec = g_stream_log.independent(stream_key(s), reads, writes) ? 1 : 0;
@@ -1723,9 +1887,7 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
     ma[0].val.programmaticStreamSerializationAllowed = 1;
     mc.attrs = ma;
     mc.numAttrs = 1;
-    const cudaError_t e = mode == kModeFast      ? cudaLaunchKernelEx(&mc, decode_attention_kernel<kModeFast>, P)
-                          : mode == kModeAdapter ? cudaLaunchKernelEx(&mc, decode_attention_kernel<kModeAdapter>, P)
-                                                 : cudaLaunchKernelEx(&mc, decode_attention_kernel<kModeGeneral>, P);
+    const cudaError_t e = pass.launch(&mc, P);
     if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_decode_attention: ") + cudaGetErrorString(e));
   }
   // Split combine as a programmatic dependent launch of the attention grid.
@@ -1764,6 +1926,30 @@ int tp_decode_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state 
   // Without a step the kernels only read the state words.
   return run_attention(pool, tail, state, const_cast<int32_t*>(d_state), q, q_dtype, num_q_heads, scale, out,
                        partial_out, workspace, workspace_bytes, stream, nullptr);
+}
+
+int tp_decode_attention_dense_v(const tp_page_pool* pool, tp_state state, const void* v, int64_t v_head_stride,
+                                int64_t v_tokens, const void* q, int32_t q_dtype, int32_t num_q_heads, float scale,
+                                void* out, float* partial_out, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  if (!pool) return fail(TP_ERR_INVALID, "page pool is NULL");
+  if (state.tail_len != 0 || state.first_page != 0)
+    return fail(TP_ERR_INVALID, "tp_decode_attention_dense_v: pages only (tail_len and first_page must be 0)");
+  if (state.n_pages < 1 || state.n_pages > pool->page_capacity)
+    return fail(TP_ERR_INVALID, "tp_decode_attention_dense_v: n_pages must be in [1, page_capacity]");
+  if (state.seq_len < 1 || int64_t(state.seq_len) > int64_t(state.n_pages) * TP_PAGE_TOKENS)
+    return fail(TP_ERR_INVALID, "tp_decode_attention_dense_v: seq_len must be in [1, 64 * n_pages]");
+  if (!v || (reinterpret_cast<uintptr_t>(v) & 15))
+    return fail(TP_ERR_INVALID, "tp_decode_attention_dense_v: the value array must be 16-byte aligned");
+  if (v_tokens < state.seq_len || v_tokens > (int64_t(1) << 31))
+    return fail(TP_ERR_INVALID, "tp_decode_attention_dense_v: v_tokens must be in [seq_len, 2^31]");
+  if (v_head_stride < v_tokens * kD || v_head_stride % 8 || v_head_stride >= (int64_t(1) << 39))
+    return fail(TP_ERR_INVALID,
+                "tp_decode_attention_dense_v: v_head_stride must be a multiple of 8, >= 128 * v_tokens and < 2^39");
+  const tp_tail none = {nullptr, nullptr, TP_F16};
+  const DenseV dv{v, v_head_stride, v_tokens};
+  return run_attention(pool, &none, state, nullptr, q, q_dtype, num_q_heads, scale, out, partial_out, workspace,
+                       workspace_bytes, stream, nullptr, nullptr, &dv);
 }
 
 int tp_decode_step(const tp_page_pool* pool, const tp_tail* tail, int32_t* d_state, const void* k_new,

@@ -60,6 +60,8 @@ struct CallBuffers {
   size_t new_bytes = 0;                // each of k_new, v_new
   const void* exchange = nullptr;      // this rank's exchange buffer (sharded call), or NULL
   size_t exchange_bytes = 0;
+  const void* values = nullptr;        // dense value array (dense-V call), read
+  size_t values_bytes = 0;
 };
 
 // What `b` reads and writes.  The workspace is left out of both sides: the page pass writes its
@@ -87,6 +89,7 @@ inline void call_spans(const CallBuffers& b, Spans& reads, Spans& writes) {
   }
   reads.add(b.exchange, b.exchange_bytes);
   writes.add(b.exchange, b.exchange_bytes);
+  reads.add(b.values, b.values_bytes);
 }
 
 // The writes a new call on a stream must not read early.  Only this library's kernels let a

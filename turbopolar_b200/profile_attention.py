@@ -9,20 +9,22 @@ time and the achieved GB/s of algorithmic bytes (compressed pages + dense tail +
 independent launches (every layer reads the same query) and for a dependent chain (each
 layer's query is the previous layer's output).
 ``--launches N`` instead issues N plain launches over the layers (for ncu: one kernel per
-launch, no graph).
+launch, no graph).  ``--dense-v`` times tp_decode_attention_dense_v instead (the keys of the
+same pages, float16 values from a separate array; no dense tail: ``--ctx`` a multiple of 64).
 """
 
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 
 import numpy as np
 import torch
 
-from . import TurboPolarConfig, TurboPolarKVCacheRuntime, build
-from .pages import page_bytes
+from . import TurboPolarConfig, TurboPolarKVCacheRuntime, _lib, build
+from .pages import page_bytes, row_bytes
 
 FORMATS = {
     "default": {},
@@ -33,21 +35,41 @@ L2_BYTES = 126 * 2 ** 20
 
 def make_layers(a, dev):
     cfg = TurboPolarConfig(num_q_heads=a.hq, num_kv_heads=a.hkv, **FORMATS[a.format])
-    per_layer = (a.ctx // 64) * a.hkv * page_bytes(cfg.format_fields())
+    per_layer = (a.ctx // 64) * a.hkv * page_bytes(cfg.format_fields()) + (a.ctx * a.hkv * 256 if a.dense_v else 0)
     n = a.layers or max(1, math.ceil(4 * L2_BYTES / max(per_layer, 1)))
     gen = torch.Generator(device=dev)
     chan = torch.from_numpy(np.random.default_rng(1).uniform(0.5, 4.0, size=128).astype(np.float32)).to(dev)
-    layers = []
+    layers, values = [], []
     for i in range(n):
         gen.manual_seed(a.seed + i)
         k = (torch.randn((1, a.hkv, a.ctx, 128), generator=gen, device=dev) * chan).half()
         v = torch.randn((1, a.hkv, a.ctx, 128), generator=gen, device=dev).half()
         rt = TurboPolarKVCacheRuntime(cfg, max_seq_len=a.ctx, check_finite=False)
         rt.append(k, v)
+        if a.dense_v:
+            values.append(v[0].contiguous())
         del k, v
         layers.append(rt)
     q = torch.randn((1, a.hq, 128), generator=gen, device=dev).half()
-    return cfg, layers, q
+    return cfg, layers, values, q
+
+
+def dense_v_caller(a, layers, values, dev):
+    """attend(i, q, out): tp_decode_attention_dense_v over layer i's pages and values."""
+    if a.ctx % 64:
+        raise SystemExit("--dense-v needs --ctx a multiple of 64")
+    lib = _lib.lib()
+    ws = [torch.zeros(lib.tp_decode_attention_workspace_size(a.hkv, a.hq), dtype=torch.uint8, device=dev)
+          for _ in layers]
+    scale = float(layers[0].config.attention_scale)
+
+    def attend(i, q, out):
+        rt = layers[i]
+        _lib.check(lib.tp_decode_attention_dense_v(
+            ctypes.byref(rt.pool_struct()), _lib.State(rt.n_pages, 0, a.ctx, 0), values[i].data_ptr(), a.ctx * 128,
+            a.ctx, q.data_ptr(), _lib.TP_F16, a.hq, scale, out.data_ptr(), None, ws[i].data_ptr(), ws[i].numel(),
+            torch.cuda.current_stream(dev).cuda_stream))
+    return attend
 
 
 def main(argv=None):
@@ -60,19 +82,31 @@ def main(argv=None):
     ap.add_argument("--launches", type=int, default=0, help="plain launches instead of graph replays")
     ap.add_argument("--format", default="default", choices=sorted(FORMATS))
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--dense-v", action="store_true", help="time tp_decode_attention_dense_v")
     a = ap.parse_args(argv)
     build.build()
     dev = torch.device("cuda:0")
-    cfg, layers, q = make_layers(a, dev)
+    cfg, layers, values, q = make_layers(a, dev)
     outs = [torch.empty((1, a.hq, 128), dtype=torch.float16, device=dev) for _ in layers]
-    for rt, o in zip(layers, outs):
-        rt.attention(q, out=o)
+    if a.dense_v:
+        attend = dense_v_caller(a, layers, values, dev)
+    else:
+        def attend(i, q, out):
+            layers[i].attention(q, out=out)
+    for i, o in enumerate(outs):
+        attend(i, q, o)
     torch.cuda.synchronize()
     rt0 = layers[0]
-    nbytes = rt0.n_pages * a.hkv * page_bytes(rt0.fmt) + rt0.tail_len * a.hkv * 128 * 4 + a.hq * 128 * 4
+    if a.dense_v:  # keys (radii + angle codes) of every page, float16 values, q, out
+        fmt = rt0.fmt
+        l1, deep = row_bytes(fmt)
+        k_row = (64 if fmt["int8_radii"] else 128) + l1 + deep
+        nbytes = rt0.n_pages * 64 * a.hkv * (k_row + 256) + a.hq * 128 * 4
+    else:
+        nbytes = rt0.n_pages * a.hkv * page_bytes(rt0.fmt) + rt0.tail_len * a.hkv * 128 * 4 + a.hq * 128 * 4
     if a.launches:
         for i in range(a.launches):
-            layers[i % len(layers)].attention(q, out=outs[i % len(layers)])
+            attend(i % len(layers), q, outs[i % len(layers)])
         torch.cuda.synchronize()
         print(json.dumps({"plain_launches": a.launches}))
         return
@@ -80,8 +114,8 @@ def main(argv=None):
     def per_launch_us(chain: bool) -> float:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            for i, (rt, o) in enumerate(zip(layers, outs)):
-                rt.attention(outs[i - 1] if chain and i > 0 else q, out=o)
+            for i, o in enumerate(outs):
+                attend(i, outs[i - 1] if chain and i > 0 else q, o)
         for _ in range(3):
             g.replay()
         torch.cuda.synchronize()
@@ -99,7 +133,8 @@ def main(argv=None):
     # one has completed).
     us = per_launch_us(False)
     dep = per_launch_us(True)
-    print(json.dumps({"ctx": a.ctx, "hq": a.hq, "hkv": a.hkv, "format": a.format, "layers": len(layers),
+    print(json.dumps({"ctx": a.ctx, "hq": a.hq, "hkv": a.hkv, "format": a.format, "dense_v": a.dense_v,
+                      "layers": len(layers),
                       "us_per_launch": us, "bytes_per_launch": nbytes, "gbs": nbytes / us / 1e3,
                       "us_per_launch_dependent": dep, "gbs_dependent": nbytes / dep / 1e3}))
 
