@@ -45,6 +45,14 @@ static bool run(StreamLog& log, const void* stream, const CallBuffers& b, int de
   return log.independent(StreamKey{device, uintptr_t(stream), thread, capture}, r, w);
 }
 
+// The decision and whether the call's cache (state words, pages, radius scales) is final.
+static bool run_probe(StreamLog& log, const void* stream, const CallBuffers& b, bool* cache_final) {
+  Spans r, w, c;
+  call_spans(b, r, w);
+  cache_spans(b, c);
+  return log.independent(StreamKey{0, uintptr_t(stream), 0, 0}, r, w, &c, cache_final);
+}
+
 #define CHECK(cond) do { if (!(cond)) { std::printf("FAIL line %d: %s\n", __LINE__, #cond); std::exit(1); } } while (0)
 
 int main() {
@@ -160,6 +168,22 @@ int main() {
       if (!run(log, s1, b)) ++waited;
     }
     CHECK(waited >= 1 && waited <= 2);
+  }
+  {  // the cache probe of a dependent call: final when no call of the chain writes that cache
+    StreamLog log;
+    bool fin = true;
+    CHECK(!run_probe(log, s1, call(0, 300000, 400000, true), &fin) && !fin);  // first call: unknown
+    // Layer B's query is layer A's output (dependent), B's cache is written by nobody running.
+    CHECK(!run_probe(log, s1, call(100000, 400000, 410000, true), &fin) && fin);
+    // Layer C's query is B's output; B's step (in the chain) wrote B's cache, not C's.
+    CHECK(!run_probe(log, s1, call(200000, 410000, 420000, false), &fin) && fin);
+    // Attention on B's cache again: B's step is no longer in the chain (it restarted at C),
+    // and C writes only its output.
+    CHECK(run_probe(log, s1, call(100000, 300000, 430000, false), &fin) && fin);
+    // A step on C's cache, then attention on it whose query is that step's output: dependent,
+    // and the step (still running, perhaps) writes the cache.
+    run_probe(log, s1, call(200000, 300000, 440000, true), &fin);
+    CHECK(!run_probe(log, s1, call(200000, 440000, 450000, false), &fin) && !fin);
   }
   {  // more ranges than fit count as overlapping everything
     Spans r, w;

@@ -104,6 +104,9 @@ struct AttnParams {
   // The previous call launched on this stream writes nothing this call reads: the page pass
   // streams before griddepcontrol.wait (the host decides: StreamLog in tp_overlap.h).
   int spec;
+  // No call that may still be running writes this call's state words, pages or radius scales:
+  // what the page pass reads of them before griddepcontrol.wait is final (StreamLog's probe).
+  int cache_final;
   // Fused decode step: one new token per KV head (k_new/v_new, tail dtype, heads
   // new_head_stride elements apart) appended before attention; wpool is the writable pool.
   int fused;
@@ -797,15 +800,16 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
     // now.  Every page below the newest one was written by a launch that had completed before
     // the previous kernel in the stream started, so copies of those are valid whatever that
     // kernel does; the newest page may be the one it is writing (an append that completed a
-    // page), so nothing is issued early if the first units touch it.
+    // page), so nothing is issued early if the first units touch it -- unless no call that
+    // may still run writes this cache (P.cache_final), when the state read above is final too.
     early = pt.active;
-    for (int k = 0; early && k < min(R, pt.n); ++k) early = unit_ref(pt, k).y < pt.n_pages - 1;
+    for (int k = 0; early && !P.cache_final && k < min(R, pt.n); ++k) early = unit_ref(pt, k).y < pt.n_pages - 1;
     if (early && issuer) produce_range(0, S);
 
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
     // Let the split-combine grid become resident now; it waits for this grid to complete.
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-    st = read_state(P);
+    if (!P.cache_final) st = read_state(P);
   }
   if (!P.spec && min(max(st.n_pages, 0), P.page_capacity) != pt.n_pages) {
     // The previous kernel appended to this cache: let the early copies land, reset the
@@ -1876,9 +1880,12 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
       b.values = dv->v;
       b.values_bytes = size_t((hkv - 1) * dv->head_stride + dv->tokens * kD) * sizeof(__half);
     }
-    Spans reads, writes;
+    Spans reads, writes, cache;
     call_spans(b, reads, writes);
-    P.spec = g_stream_log.independent(stream_key(s), reads, writes) ? 1 : 0;
+    cache_spans(b, cache);
+    bool cache_final = false;
+    P.spec = g_stream_log.independent(stream_key(s), reads, writes, &cache, &cache_final) ? 1 : 0;
+    P.cache_final = cache_final ? 1 : 0;
   }
   // The page pass is a programmatic dependent of whatever precedes it in the stream (a no-op
   // unless that kernel triggers early, as the split combine of a previous call does): its

@@ -64,6 +64,13 @@ struct CallBuffers {
   size_t values_bytes = 0;
 };
 
+// The cache a page pass reads before griddepcontrol.wait: state words, pages, radius scales.
+inline void cache_spans(const CallBuffers& b, Spans& out) {
+  out.add(b.d_state, b.state_bytes);
+  out.add(b.pages, b.pages_bytes);
+  out.add(b.radii_scales, b.radii_scales_bytes);
+}
+
 // What `b` reads and writes.  The workspace is left out of both sides: the page pass writes its
 // partials only after griddepcontrol.wait, and the split combine reads them after its own.  A
 // sharded call's split combine reads and advances the epoch in this rank's exchange buffer
@@ -155,9 +162,13 @@ class StreamLog {
  public:
   // True when this call may read early: the stream has a chain and nothing its calls write is
   // read by this call.  Adds this call's writes to the chain, or restarts the chain with them.
-  bool independent(const StreamKey& key, const Spans& reads, const Spans& writes) {
+  // With `probe`, *probe_clear tells whether the chain (before this call) writes none of the
+  // probe's ranges: what a dependent call reads of them before its wait is then final too.
+  bool independent(const StreamKey& key, const Spans& reads, const Spans& writes, const Spans* probe = nullptr,
+                   bool* probe_clear = nullptr) {
     std::lock_guard<std::mutex> lock(mu_);
     auto it = last_.find(key);
+    if (probe_clear) *probe_clear = it != last_.end() && !it->second.meets(*probe);
     if (it == last_.end()) {
       if (key.capture != 0) {
         for (auto j = last_.begin(); j != last_.end();) {
