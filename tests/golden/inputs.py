@@ -90,3 +90,22 @@ def prefill_inputs():
     kp2 = rng.standard_normal((1, 2, 30, 128)).astype(np.float16)
     vp2 = rng.standard_normal((1, 2, 30, 128)).astype(np.float16)
     return kp, vp, kp2, vp2
+
+
+DENSE_V_CASES = {
+    # name: (TurboPolarConfig overrides, seed); 8 query / 2 KV heads, 192 tokens (3 pages)
+    "default": ({}, 31),
+    "adapter_fmt": (dict(use_int8_radii=True, k_angle_bits_deep=8, split_dim=0), 32),
+}
+DENSE_V_LENGTHS = (192, 150, 70)
+
+
+def dense_v_inputs(name: str):
+    """K ``(1,2,192,128)`` fp16 (N(0,1) times the channel scale), V ``(1,2,192,128)`` fp16 and a
+    query ``(1,8,128)`` fp16, N(0,1)."""
+    _, seed = DENSE_V_CASES[name]
+    rng = np.random.default_rng(seed)
+    k = (rng.standard_normal((1, 2, 192, 128)).astype(np.float32) * channel_scale()).astype(np.float16)
+    v = rng.standard_normal((1, 2, 192, 128)).astype(np.float16)
+    q = rng.standard_normal((1, 8, 128)).astype(np.float16)
+    return k, v, q

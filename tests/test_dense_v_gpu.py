@@ -6,7 +6,8 @@ keys and the values as given.
 Cases: every key-format path of the page pass (the table-driven default format, the adapter
 format, the general path with 8-bit level-1 / 2-bit deep codes and with int8 radii), GQA groups
 1 to 8, masking of the last tokens, a 5-D value block, batch 2, a value array shorter than the
-pages (read as zeros past its end), and 32K tokens at the Llama-3 head layout.
+pages (read as zeros past its end), 32K tokens at the Llama-3 head layout, and the outputs of
+the reference's own code (``tests/golden/dense_v.npz``).
 """
 
 import ctypes
@@ -144,3 +145,29 @@ def test_dense_v_32k_vs_float64(fmt):
             want[4 * h:4 * h + 4] = torch.softmax(s, dim=-1) @ v[0, h, :L].double()
         err = float((out[0].double() - want).abs().max())
         assert err < ATOL, (L, err)
+
+
+@pytest.mark.parametrize("name", ["default", "adapter_fmt"])
+def test_dense_v_vs_reference_fixture(name):
+    """Against the reference's own execute_online_attention_dense_v (tests/golden/dense_v.npz, its
+    CPU fallback in float16): the kernel is within ATOL of the float64 oracle, and within the
+    reference's float16 error (4e-3, the bound the oracle itself needs) of the fixture."""
+    import os
+
+    import inputs
+    from turbopolar_b200 import CudaKernelBridge
+    g = np.load(os.path.join(os.path.dirname(inputs.__file__), "dense_v.npz"))
+    overrides, _ = inputs.DENSE_V_CASES[name]
+    cfg = _cfg(num_q_heads=8, num_kv_heads=2, **overrides)
+    k, v, q = inputs.dense_v_inputs(name)
+    _, blk = _cache(cfg, k, v)
+    # The pages hold the reference runtime's codes.
+    for f in ("radii", "angle_codes_l1", "angle_codes_deep"):
+        np.testing.assert_array_equal(getattr(blk, f).cpu().numpy(), g[f"{name}/{f}"])
+    pages, _, _ = oracle_cache(k, v, fmt_of(cfg), cfg.use_int8_radii)
+    for length in inputs.DENSE_V_LENGTHS:
+        out, _ = CudaKernelBridge().execute_online_attention_dense_v(T(q), blk, T(v), None, None, cfg, length)
+        got = out.float().cpu().numpy()[0].astype(np.float64)
+        want = oatt.attention_dense_v(q[0].astype(np.float64), pages, fmt_of(cfg), v[0], length, cfg.attention_scale)
+        assert np.max(np.abs(got - want)) < ATOL, length
+        assert np.max(np.abs(got - g[f"{name}/out_L{length}"][0].astype(np.float64))) < 4e-3, length

@@ -165,3 +165,56 @@ def test_prefill_decompress_on_read(golden):
     k2, v2 = _oracle_prefill(np.concatenate([kp, kp2], axis=2), np.concatenate([vp, vp2], axis=2))
     for got, key in ((k1, "k_out"), (v1, "v_out"), (k2, "k_out2"), (v2, "v_out2")):
         np.testing.assert_array_equal(got.view(np.uint16), golden[f"prefill/{key}"].view(np.uint16))
+
+
+def _fallback_fp16(q, kd, v, length, scale):
+    """``_cpu_online_attention`` (``metal.py:267-291``, entered from ``metal.py:597-603``) as the
+    reference evaluates it on float16 arrays (the fixtures' MLX stand-in: each float16 product
+    rounded once, float16 sums accumulated in float32, softmax in float32 rounded back, the
+    -1e9 mask a float16 -inf).  q (H_q,128), kd, v (H_kv,T,128) float16."""
+    f32 = np.float32
+    g = q.shape[0] // kd.shape[0]
+    kk = np.repeat(kd, g, axis=0)
+    prod = (q[:, None, :].astype(f32) * kk.astype(f32)).astype(np.float16)
+    s = prod.astype(f32).sum(-1).astype(np.float16)
+    s = (s.astype(f32) * f32(np.float16(scale))).astype(np.float16)
+    s = np.where(np.arange(s.shape[-1])[None, :] < length, s, np.float16(-np.inf))
+    a = s.astype(f32)
+    e = np.exp((a - a.max(-1, keepdims=True)).astype(np.float64)).astype(f32)
+    w = (e / e.sum(-1, keepdims=True)).astype(np.float16)
+    vv = np.repeat(v, g, axis=0)
+    return (w[:, :, None].astype(f32) * vv.astype(f32)).astype(np.float16).astype(f32).sum(1).astype(np.float16)
+
+
+@pytest.mark.parametrize("name", list(inputs.DENSE_V_CASES))
+def test_dense_v_attention_vs_reference(name):
+    """The oracle's attention_dense_v against the reference's execute_online_attention_dense_v
+    fallback (dense_v.npz, made by make_golden_dense_v.py): the keys the reference's runtime
+    encoded, bit for bit, and the output at every masked length."""
+    import os
+    g = np.load(os.path.join(os.path.dirname(inputs.__file__), "dense_v.npz"))
+    overrides, _ = inputs.DENSE_V_CASES[name]
+    fmt = _fmt(overrides)
+    k, v, q = inputs.dense_v_inputs(name)
+    kb = k[0].reshape(2, 3, 64, 128)
+    enc = polar.encode_block(kb, int8_radii=overrides.get("use_int8_radii", False), **fmt)
+    for f in ("radii", "angle_codes_l1", "angle_codes_deep"):
+        np.testing.assert_array_equal(enc[f], g[f"{name}/{f}"][0])
+    rs = None
+    if overrides.get("use_int8_radii"):
+        rs = enc["radii_scales"][..., 0, 0]
+        np.testing.assert_array_equal(rs.reshape(-1), g[f"{name}/radii_scales"].reshape(-1))
+    pages = dict(radii=enc["radii"], angle_codes_l1=enc["angle_codes_l1"], angle_codes_deep=enc["angle_codes_deep"],
+                 radii_scales=rs, v_codes=np.zeros((2, 3, 64, 128), np.int8), v_scales=np.zeros((2, 3, 64, 4), np.float16))
+    kd, _ = attention.decode_pages(pages, fmt)
+    scale = 1 / np.sqrt(128)
+    for length in inputs.DENSE_V_LENGTHS:
+        ref = g[f"{name}/out_L{length}"][0]
+        # The oracle's formula evaluated with the reference's float16 roundings: the same output.
+        emu = _fallback_fp16(q[0], kd.astype(np.float16), v[0], length, scale)
+        np.testing.assert_array_equal(emu.view(np.uint16), ref.view(np.uint16))
+        # The oracle itself (float64) lies within the reference's own float16 error of it
+        # (measured 2.2e-3 to 3.5e-3; most of it is the float16 rounding of the raw scores q.k,
+        # tens in magnitude with these channel-scaled keys).
+        out = attention.attention_dense_v(q[0].astype(np.float64), pages, fmt, v[0], length, scale)
+        assert np.max(np.abs(out - ref.astype(np.float64))) < 4e-3, length
