@@ -12,6 +12,39 @@ def _fmt(overrides):
                 split_dim=overrides.get("split_dim", 64))
 
 
+def _fallback_fp16(q, kd, v, length, scale):
+    """``_cpu_online_attention`` (``metal.py:267-291``, entered from ``metal.py:597-603``) as the
+    reference evaluates it on float16 arrays (the fixtures' MLX stand-in: each float16 product
+    rounded once, float16 sums accumulated in float32, softmax in float32 rounded back, the
+    -1e9 mask a float16 -inf).  q (H_q,128), kd, v (H_kv,T,128) float16."""
+    f32 = np.float32
+    g = q.shape[0] // kd.shape[0]
+    kk = np.repeat(kd, g, axis=0)
+    prod = (q[:, None, :].astype(f32) * kk.astype(f32)).astype(np.float16)
+    s = prod.astype(f32).sum(-1).astype(np.float16)
+    s = (s.astype(f32) * f32(np.float16(scale))).astype(np.float16)
+    s = np.where(np.arange(s.shape[-1])[None, :] < length, s, np.float16(-np.inf))
+    a = s.astype(f32)
+    e = np.exp((a - a.max(-1, keepdims=True)).astype(np.float64)).astype(f32)
+    w = (e / e.sum(-1, keepdims=True)).astype(np.float16)
+    vv = np.repeat(v, g, axis=0)
+    return (w[:, :, None].astype(f32) * vv.astype(f32)).astype(np.float16).astype(f32).sum(1).astype(np.float16)
+
+
+def _cache_fp16(pages, fmt, tail_k, tail_v):
+    """Keys and values the reference's fallback attends over: decoded pages then the dense tail,
+    float16 ``(H_kv, T, 128)`` (``metal.py:293-312``)."""
+    ks, vs = [], []
+    if pages is not None and np.asarray(pages["radii"]).shape[1] > 0:
+        k, v = attention.decode_pages(pages, fmt)
+        ks.append(k)
+        vs.append(v)
+    if tail_k is not None and tail_k.shape[1] > 0:
+        ks.append(tail_k)
+        vs.append(tail_v)
+    return np.concatenate(ks, 1).astype(np.float16), np.concatenate(vs, 1).astype(np.float16)
+
+
 @pytest.mark.parametrize("name", list(inputs.CODEC_CASES))
 def test_codec_bit_exact(name, golden):
     overrides, _, _ = inputs.CODEC_CASES[name]
@@ -60,7 +93,11 @@ def test_c1_runtime_and_fallback_attention(golden, golden_meta):
     fmt = model.fmt
     out = attention.attention_dense_tail(q[0], pages, fmt, model.partial_k[0], model.partial_v[0], 100, 1 / np.sqrt(128))
     ref = golden["c1/out"][0].astype(np.float64)
-    # The reference fallback reduces in float16; the oracle in float64.
+    # The oracle's formula with the reference's float16 roundings gives the reference's output
+    # bit for bit; the oracle itself (float64) is within the reference's float16 error of it.
+    kk, vv = _cache_fp16(pages, fmt, model.partial_k[0], model.partial_v[0])
+    emu = _fallback_fp16(q[0], kk, vv, 100, 1 / np.sqrt(128))
+    np.testing.assert_array_equal(emu.view(np.uint16), golden["c1/out"][0].view(np.uint16))
     assert np.max(np.abs(out - ref)) < 2e-3
     k_dec, _ = attention.decode_pages(pages, fmt)
     sc = attention.fused_scores(q[0], k_dec, 1 / np.sqrt(128))
@@ -126,7 +163,8 @@ def test_codec_known_answers():
 
 def test_adapter_sequence_oracle(golden):
     """Oracle attention over the cache contents after every decode step agrees with the
-    reference adapter's outputs (dense-only, compressed+tail and block-boundary branches)."""
+    reference adapter's outputs (dense-only, compressed+tail and block-boundary branches of
+    turbopolar_fast_attention.py:145-188, which all evaluate the same formula)."""
     qs, ks, vs = inputs.adapter_inputs()
     for name, overrides in inputs.ADAPTER_CASES.items():
         fmt = _fmt(overrides)
@@ -138,6 +176,11 @@ def test_adapter_sequence_oracle(golden):
             tk = model.partial_k[0] if model.partial_k is not None else None
             tv = model.partial_v[0] if model.partial_v is not None else None
             out = attention.attention_dense_tail(qs[i][0, :, 0, :], pages, fmt, tk, tv, i + 1, 1 / np.sqrt(128))
+            # Bit for bit with the reference's float16 evaluation of the same formula at every
+            # step; the float64 oracle within the reference's float16 error (measured 2.03e-3).
+            kk, vv = _cache_fp16(pages, fmt, tk, tv)
+            emu = _fallback_fp16(qs[i][0, :, 0, :], kk, vv, i + 1, 1 / np.sqrt(128))
+            np.testing.assert_array_equal(emu.view(np.uint16), want[i][0].view(np.uint16), err_msg=f"{name} {i}")
             assert np.max(np.abs(out - want[i][0].astype(np.float64))) < 3e-3, (name, i)
 
 
@@ -165,25 +208,6 @@ def test_prefill_decompress_on_read(golden):
     k2, v2 = _oracle_prefill(np.concatenate([kp, kp2], axis=2), np.concatenate([vp, vp2], axis=2))
     for got, key in ((k1, "k_out"), (v1, "v_out"), (k2, "k_out2"), (v2, "v_out2")):
         np.testing.assert_array_equal(got.view(np.uint16), golden[f"prefill/{key}"].view(np.uint16))
-
-
-def _fallback_fp16(q, kd, v, length, scale):
-    """``_cpu_online_attention`` (``metal.py:267-291``, entered from ``metal.py:597-603``) as the
-    reference evaluates it on float16 arrays (the fixtures' MLX stand-in: each float16 product
-    rounded once, float16 sums accumulated in float32, softmax in float32 rounded back, the
-    -1e9 mask a float16 -inf).  q (H_q,128), kd, v (H_kv,T,128) float16."""
-    f32 = np.float32
-    g = q.shape[0] // kd.shape[0]
-    kk = np.repeat(kd, g, axis=0)
-    prod = (q[:, None, :].astype(f32) * kk.astype(f32)).astype(np.float16)
-    s = prod.astype(f32).sum(-1).astype(np.float16)
-    s = (s.astype(f32) * f32(np.float16(scale))).astype(np.float16)
-    s = np.where(np.arange(s.shape[-1])[None, :] < length, s, np.float16(-np.inf))
-    a = s.astype(f32)
-    e = np.exp((a - a.max(-1, keepdims=True)).astype(np.float64)).astype(f32)
-    w = (e / e.sum(-1, keepdims=True)).astype(np.float16)
-    vv = np.repeat(v, g, axis=0)
-    return (w[:, :, None].astype(f32) * vv.astype(f32)).astype(np.float16).astype(f32).sum(1).astype(np.float16)
 
 
 @pytest.mark.parametrize("name", list(inputs.DENSE_V_CASES))
