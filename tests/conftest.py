@@ -34,3 +34,20 @@ def has_cuda():
         return torch.cuda.is_available()
     except Exception:
         return False
+
+
+@pytest.fixture(autouse=True)
+def _guard_bytes(request):
+    """GPU tests run with canary guard bytes around the runtime's device buffers (page pools,
+    radius scales, dense tails, state words; turbopolar_b200.guard) and check them afterwards:
+    a kernel write past any of those buffers fails the test that made it."""
+    if request.node.get_closest_marker("gpu") is None or not has_cuda():
+        yield
+        return
+    from turbopolar_b200 import guard
+    guard.enable(4096)
+    try:
+        yield
+        guard.check()
+    finally:
+        guard.disable()

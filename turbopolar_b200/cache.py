@@ -28,7 +28,7 @@ from typing import Any, Dict, Optional, Tuple
 
 import torch
 
-from . import _lib
+from . import _lib, guard
 from .codec import encode_pages, _stream
 from .config import TurboPolarConfig
 from .pages import PAGE, PagePool, page_bytes
@@ -131,9 +131,9 @@ class TurboPolarKVCacheRuntime:
 
     def _allocate_tail(self):
         dev = self.device
-        self.tail_k = torch.zeros((self.heads, PAGE, 128), dtype=self._input_dtype, device=dev)
-        self.tail_v = torch.zeros_like(self.tail_k)
-        self.d_state = torch.zeros(_lib.STATE_WORDS, dtype=torch.int32, device=dev)
+        self.tail_k = guard.zeros((self.heads, PAGE, 128), self._input_dtype, dev, "dense tail (K)")
+        self.tail_v = guard.zeros((self.heads, PAGE, 128), self._input_dtype, dev, "dense tail (V)")
+        self.d_state = guard.zeros((_lib.STATE_WORDS,), torch.int32, dev, "state words")
         if self.first_page:
             self.d_state[2] = self.first_page * PAGE
             self.d_state[3] = self.first_page

@@ -16,7 +16,7 @@ import ctypes
 
 import torch
 
-from . import _lib
+from . import _lib, guard
 
 PAGE = 64
 HEAD_DIM = 128
@@ -104,8 +104,8 @@ class PagePool:
         self.heads, self.capacity, self.fmt, self.device = heads, capacity, dict(fmt), torch.device(device)
         self.l1_row, self.deep_row = row_bytes(self.fmt)
         self.unit_bytes = unit_bytes(self.fmt)
-        self.pages = torch.zeros((heads, capacity, 2 * self.unit_bytes), dtype=torch.uint8, device=self.device)
-        self.radii_scales = (torch.zeros((heads, capacity), dtype=torch.float16, device=self.device)
+        self.pages = guard.zeros((heads, capacity, 2 * self.unit_bytes), torch.uint8, self.device, "page pool")
+        self.radii_scales = (guard.zeros((heads, capacity), torch.float16, self.device, "radius scales")
                              if fmt["int8_radii"] else None)
         self._struct = None
 
@@ -135,6 +135,10 @@ class PagePool:
     def grown(self, new_capacity: int, n_valid: int) -> "PagePool":
         """A larger pool holding a device copy of the first ``n_valid`` pages of every head."""
         new = PagePool(self.heads, new_capacity, self.fmt, self.device)
+        if guard.enabled():  # this pool is dropped once the copy is taken
+            guard.check_tensor(self.pages)
+            if self.radii_scales is not None:
+                guard.check_tensor(self.radii_scales)
         if n_valid:
             new.pages[:, :n_valid].copy_(self.pages[:, :n_valid])
             if self.radii_scales is not None:
