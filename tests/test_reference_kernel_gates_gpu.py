@@ -2,7 +2,8 @@
 
 ``tests/benchmarks/test_turbo_polar_kernel_qk.py`` (``test_phase_6_fused_qk_precision``) and
 ``tests/benchmarks/test_turbo_polar_online_attention.py`` (``test_phase_8_dense_v_gate``,
-``test_phase_9_quant_v_gate``, ``test_long_context_float_accumulator_stability``): the same
+``test_phase_9_quant_v_gate``, ``test_long_context_float_accumulator_stability``), and
+``tests/benchmarks/test_turbopolar_fast_attention.py`` (the Llama adapter's three decode cases): the same
 configurations, shapes, reference formula (scores over the decoded keys, softmax, weighted sum
 of the values) and gates (max error and cosine).  The QJL variants are left out (QJL is rejected
 by the configuration contract).  Inputs: seeded NumPy float32 normals in place of
@@ -125,3 +126,36 @@ def test_long_context_float_accumulator_stability(t):
     err, cosine = _gates(_reference_attention(cfg, q, unified, v), got)
     assert err <= 2e-3 * np.sqrt(t / 64.0) and cosine >= 0.999, (err, cosine)
     assert err <= 2e-3, err
+
+
+# tests/benchmarks/test_turbopolar_fast_attention.py: the Llama adapter's decode_attention.  As
+# in the reference, the ground truth is dense attention over the tokens appended before the last
+# call (which appends one more), with its cosine gates.
+@pytest.mark.parametrize("tokens,seed,gate", [(37, 2026, 0.99), (100, 2027, 0.95), (64, 2028, 0.95)])
+def test_fast_attention_decode_vs_dense_history(tokens, seed, gate):
+    """:21-61 (all tokens in the dense tail), :63-103 (one compressed block and a tail),
+    :105-141 (ending on a block boundary)."""
+    from turbopolar_b200 import TurboPolarConfig
+    from turbopolar_b200.llama import TurboPolarFastCache
+    cfg = TurboPolarConfig(head_dim=128, block_size=64, num_q_heads=4, num_kv_heads=2, storage_mode="kv_quant",
+                           use_int8_radii=True)
+    cache = TurboPolarFastCache(cfg)
+    scale = cfg.attention_scale
+    rng = np.random.default_rng(seed)
+    ks, vs = [], []
+    for _ in range(tokens):
+        q = _normal(rng, (1, 4, 1, 128))
+        k_new = _normal(rng, (1, 2, 1, 128))
+        v_new = _normal(rng, (1, 2, 1, 128))
+        ks.append(k_new)
+        vs.append(v_new)
+        out = cache.decode_attention(q, k_new, v_new, scale)
+        assert out.shape == (1, 4, 128) and not bool(torch.isnan(out).any())
+    full_k = torch.repeat_interleave(torch.cat(ks, 2), 2, dim=1).double()
+    full_v = torch.repeat_interleave(torch.cat(vs, 2), 2, dim=1).double()
+    q_last = _normal(rng, (1, 4, 1, 128))
+    w = torch.softmax((q_last.double() * full_k).sum(-1) * scale, dim=-1)
+    ref = (w[:, :, :, None] * full_v).sum(-2)
+    got = cache.decode_attention(q_last, _normal(rng, (1, 2, 1, 128)), _normal(rng, (1, 2, 1, 128)), scale)
+    _, cosine = _gates(ref, got)
+    assert cosine >= gate, cosine
