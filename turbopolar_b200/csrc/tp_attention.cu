@@ -84,7 +84,7 @@ constexpr int kHalf = 32;     // tokens per unit
 constexpr int kRecFloats = 132;
 constexpr int kPartialStride = kMaxHeads * kRecFloats;  // floats per workspace slot
 constexpr int kLutEntries = 256;
-constexpr int kMaxContrib = 192;  // CTAs that can share one head (grid <= kMaxContrib)
+constexpr int kMaxContrib = 192;  // CTAs that can share one (KV head, query chunk) segment
 
 struct AttnParams {
   const uint8_t* pages;
@@ -1571,10 +1571,14 @@ static cudaError_t reserve_smem(int variant, const void* page_pass, int smem) {
   return e;
 }
 
+// Page-pass CTAs: one per SM, or, with more (KV head, query chunk) segments than SMs (large
+// batches), whole waves of them: every SM then streams the same number of units, and a segment's
+// units span at most three CTAs (the grid is below twice the segment count).
 static int grid_size(int num_kv_heads, int num_q_heads) {
   const int group = num_q_heads / num_kv_heads;
   const int nqc = (group + kMaxHeads - 1) / kMaxHeads;
-  return max(num_sms(), num_kv_heads * nqc);
+  const int sms = num_sms(), segs = num_kv_heads * nqc;
+  return segs <= sms ? sms : sms * ((segs + sms - 1) / sms);
 }
 
 // float32 (cos, sin) of the decoder angle of a `bits`-bit code, on the host: the angle is
@@ -1765,7 +1769,10 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
   P.partial_out = partial_out;
   const int grid = grid_size(hkv, num_q_heads);
   P.main_grid = grid;
-  if (grid > kMaxContrib) return fail(TP_ERR_UNSUPPORTED, "tp_decode_attention: too many KV heads for one launch");
+  // CTAs sharing one segment: up to the grid when it is one wave (no more segments than SMs),
+  // at most three beyond (each CTA then holds between half a segment and one segment).
+  if (hkv * P.nqc <= num_sms() && grid > kMaxContrib)
+    return fail(TP_ERR_UNSUPPORTED, "tp_decode_attention: more SMs than one head's partials can merge");
   P.ws_error = static_cast<int*>(workspace);  // word 0: error
   P.fused = step != nullptr;
   P.k_new = step ? step->k_new : nullptr;
