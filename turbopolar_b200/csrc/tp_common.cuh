@@ -237,7 +237,7 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32
       : "memory");
 }
 
-// Tiled 3-D tensor copy global -> shared (TMA, no multicast) of the box at element coordinates
+// Tiled 3-D tensor copy global -> this CTA's shared memory (TMA) of the box at element coordinates
 // (x, y, z) of the tensor map at generic address `tmap`, completing on `bar`.  x times the
 // element size must be a multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar,
