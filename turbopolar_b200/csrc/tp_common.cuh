@@ -214,7 +214,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return done != 0;
 }
-// 1-D bulk copy global -> shared completing on `bar` (no multicast).  16-byte aligned, size % 16 == 0.
+// 1-D bulk copy global -> this CTA's shared memory completing on `bar`.  16-byte aligned, size % 16 == 0.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
                    smem_u32(dst)),
