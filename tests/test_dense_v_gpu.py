@@ -171,3 +171,23 @@ def test_dense_v_vs_reference_fixture(name):
         want = oatt.attention_dense_v(q[0].astype(np.float64), pages, fmt_of(cfg), v[0], length, cfg.attention_scale)
         assert np.max(np.abs(got - want)) < ATOL, length
         assert np.max(np.abs(got - g[f"{name}/out_L{length}"][0].astype(np.float64))) < 4e-3, length
+
+
+@pytest.mark.parametrize("B", [40, 64])
+def test_dense_v_large_batches(B):
+    """40 and 64 sequences x 4 KV heads: 160 segments (two waves of the flat partition) and 256
+    (whole segments per CTA), more than the SMs; every sequence against the oracle."""
+    from turbopolar_b200 import CudaKernelBridge
+    cfg = _cfg(num_q_heads=8, num_kv_heads=4)
+    t = 192
+    k, v = kv_inputs(640, 4 * B, t, np.float16)
+    kb, vb = k.reshape(B, 4, t, 128), v.reshape(B, 4, t, 128)
+    _, blk = _cache(cfg, kb, vb)
+    pages, _, _ = oracle_cache(k, v, fmt_of(cfg), False)
+    kd, _ = oatt.decode_pages(pages, fmt_of(cfg))
+    q = np.random.default_rng(641).standard_normal((B, 8, 128)).astype(np.float16)
+    out, _ = CudaKernelBridge().execute_online_attention_dense_v(T(q), blk, T(vb), None, None, cfg, 150)
+    got = out.float().cpu().numpy()
+    for b in range(B):
+        want = oatt.attention(q[b].astype(np.float64), kd[4 * b:4 * b + 4], vb[b], 150, cfg.attention_scale)
+        assert np.max(np.abs(got[b] - want)) < ATOL, b

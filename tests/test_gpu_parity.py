@@ -365,26 +365,36 @@ def test_batch_two_flattens_heads():
         assert np.max(np.abs(out[b] - want)) < ATOL
 
 
-@pytest.mark.parametrize("batch", [24, 25, 40])
-def test_large_batches_vs_oracle(batch):
-    """Batches of 24, 25 and 40 sequences x 8 KV heads (192, 200 and 320 flattened heads: one
-    launch of whole waves of page-pass CTAs beyond 148 segments): every sequence matches the
-    oracle, for attention and for a decode step."""
+ADAPTER_FMT = dict(use_int8_radii=True, k_angle_bits_deep=8, split_dim=0)
+
+
+@pytest.mark.parametrize("batch,t,fmt", [(18, 85, {}), (24, 85, {}), (25, 85, {}), (40, 581, {}), (40, 191, {}),
+                                         (128, 300, {}), (64, 581, {}), (40, 191, ADAPTER_FMT),
+                                         (64, 191, ADAPTER_FMT),
+                                         (30, 200, dict(k_angle_bits_level1=8, k_angle_bits_deep=2, split_dim=32)),
+                                         (20, 200, dict(k_angle_bits_level1=8, k_angle_bits_deep=2, split_dim=32))])
+def test_large_batches_vs_oracle(batch, t, fmt):
+    """Batches of sequences x 8 KV heads: 144 segments (the flat partition), then 160 to 1024
+    segments, more than the 148 SMs (whole waves of the flat partition for 160, 192, 200 and 320;
+    whole segments per CTA for 240, 512 and 1024).  Contexts of one page
+    (warps without a unit in a segment), nine pages, and a decode step that completes a page
+    (191 + 1 tokens); the default, adapter and general key formats.  Every sequence matches the
+    oracle, for attention and for the step."""
     from turbopolar_b200 import TurboPolarKVCacheRuntime
-    cfg = _cfg(num_q_heads=32, num_kv_heads=8)
-    t = 64 + 21  # a page and a ragged tail
-    k, v = kv_inputs(190 + batch, 8 * batch, t + 1, np.float16)
+    cfg = _cfg(num_q_heads=32, num_kv_heads=8, **fmt)
+    k, v = kv_inputs(190 + batch + t, 8 * batch, t + 1, np.float16)
     kb, vb = k.reshape(batch, 8, t + 1, 128), v.reshape(batch, 8, t + 1, 128)
-    q = np.random.default_rng(193 + batch).standard_normal((batch, 32, 128)).astype(np.float16)
+    q = np.random.default_rng(193 + batch + t).standard_normal((batch, 32, 128)).astype(np.float16)
     rt = TurboPolarKVCacheRuntime(cfg, max_seq_len=t + 1)
     rt.append(T(kb[:, :, :t]), T(vb[:, :, :t]))
     out = N(rt.attention(T(q))).astype(np.float64)
     step = N(rt.decode_step(T(kb[:, :, t:]), T(vb[:, :, t:]), T(q))).astype(np.float64)
     assert rt.read_device_error() == 0
     for b in range(batch):
-        want = oracle_attention(q[b], kb[b:b + 1, :, :t], vb[b:b + 1, :, :t], fmt_of(cfg), False, cfg.attention_scale)
+        want = oracle_attention(q[b], kb[b:b + 1, :, :t], vb[b:b + 1, :, :t], fmt_of(cfg), cfg.use_int8_radii,
+                                cfg.attention_scale)
         assert np.max(np.abs(out[b] - want)) < ATOL, b
-        want = oracle_attention(q[b], kb[b:b + 1], vb[b:b + 1], fmt_of(cfg), False, cfg.attention_scale)
+        want = oracle_attention(q[b], kb[b:b + 1], vb[b:b + 1], fmt_of(cfg), cfg.use_int8_radii, cfg.attention_scale)
         assert np.max(np.abs(step[b] - want)) < ATOL, b
 
 

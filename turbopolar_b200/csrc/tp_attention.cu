@@ -101,6 +101,9 @@ struct AttnParams {
   int q_f32;
   int num_q_heads, num_kv_heads, group, nqc, gmax;
   int main_grid;  // CTAs of the page pass
+  // Whole-segment partition (more (KV head, query chunk) segments than CTAs): CTA c streams
+  // whole segments and writes one merged record per segment, at workspace slot = segment.
+  int owner;
   // The previous call launched on this stream writes nothing this call reads: the page pass
   // streams before griddepcontrol.wait (the host decides: StreamLog in tp_overlap.h).
   int spec;
@@ -650,16 +653,33 @@ __device__ __forceinline__ tp_state read_state(const AttnParams& P) {
 
 // This CTA's share of the page pass: units (half pages, head-major) [u0, u1) spanning at most
 // two heads ("segments"): n units, the first n0 of segment 0 (head vh_first) starting at its
-// unit a0, the rest of segment 1 starting at its unit 0.
+// unit a0, the rest of segment 1 starting at its unit 0.  Whole-segment partition (kOwner, more
+// segments than CTAs): segments [vh_first, vh_first + nseg), all of their units.
 struct Part {
   int n_pages;
   bool active;
   int vh_first, nseg, n, n0, a0;
 };
 
+template <bool kOwner>
 __device__ __forceinline__ Part make_part(const AttnParams& P, const tp_state& st, int c) {
   Part pt = {};
   pt.n_pages = min(max(st.n_pages, 0), P.page_capacity);
+  if (kOwner) {
+    // CTA c owns segments [floor(c*V/G), floor((c+1)*V/G)), V = k*G + r as in part_begin.
+    Grid g;
+    g.U = P.num_kv_heads * P.nqc;
+    g.C = int(gridDim.x);
+    g.k = g.U / g.C;
+    g.r = g.U - g.k * g.C;
+    pt.vh_first = part_begin(g, c);
+    pt.nseg = part_begin(g, c + 1) - pt.vh_first;
+    pt.active = pt.n_pages > 0 && pt.nseg > 0;
+    pt.n = pt.nseg * 2 * pt.n_pages;
+    pt.n0 = 2 * pt.n_pages;
+    pt.a0 = 0;
+    return pt;
+  }
   const Grid g = grid_of(P.num_kv_heads * P.nqc, pt.n_pages, int(gridDim.x));
   const int uph = g.uph;
   pt.active = g.U > 0 && c < g.C;
@@ -702,7 +722,7 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity) { retu
 #else
 #define TP_PAGE_PASS_REGS 192
 #endif
-template <int kMode, bool kDenseV>
+template <int kMode, bool kDenseV, bool kOwner>
 __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __grid_constant__ AttnParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr bool kExactPV = exact_pv<kMode, kDenseV>();
@@ -763,8 +783,23 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
     s_pre = st0;
   }
   __syncthreads();  // barriers initialised and the state read before any producer issues
-  Part pt = make_part(P, s_pre, c);
+  Part pt = make_part<kOwner>(P, s_pre, c);
   bool timed_out = false;
+  // Units of consumer w, and its q-th unit as (segment, page, half).  The flat partition deals
+  // CTA units w, w + kConsumers, ...; the whole-segment partition deals each segment's units
+  // w, w + kConsumers, ... < 2 * n_pages, segment after segment.
+  auto per_segment = [&](int w) { return w < 2 * pt.n_pages ? (2 * pt.n_pages - 1 - w) / kConsumers + 1 : 0; };
+  auto units_of = [&](int w) {
+    if (kOwner) return pt.nseg * per_segment(w);
+    return pt.n > w ? (pt.n - 1 - w) / kConsumers + 1 : 0;
+  };
+  auto unit_at = [&](int w, int q) {
+    if (kOwner) {
+      const int nw = per_segment(w), seg = q / nw, ui = w + kConsumers * (q - seg * nw);
+      return make_int3(seg, ui >> 1, ui & 1);
+    }
+    return unit_ref(pt, w + kConsumers * q);
+  };
   // Issue the j-th unit of consumer w (issuing lanes only).  After a release wait runs out
   // nothing more is issued (the consumers' own bounded waits then run out and return).
   auto produce = [&](int w, int j) {
@@ -773,7 +808,7 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
       timed_out = true;
       return;
     }
-    const int3 u = unit_ref(pt, w + kConsumers * j);
+    const int3 u = unit_at(w, j);
     const int kvh = (pt.vh_first + u.x) / P.nqc;
     // The unit's radius scale travels beside its copy: stored before the arrival on the
     // stage's full barrier, which releases it to the consumer.
@@ -784,7 +819,8 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
   };
   // Units [j0, j1) of the consumer this lane serves.
   auto produce_range = [&](int j0, int j1) {
-    for (int j = j0; j < j1 && pcons + kConsumers * j < pt.n && !timed_out; ++j) produce(pcons, j);
+    const int nu = units_of(pcons);
+    for (int j = j0; j < j1 && j < nu && !timed_out; ++j) produce(pcons, j);
   };
   bool early = false;
   tp_state st = s_pre;
@@ -803,7 +839,8 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
     // page), so nothing is issued early if the first units touch it -- unless no call that
     // may still run writes this cache (P.cache_final), when the state read above is final too.
     early = pt.active;
-    for (int k = 0; early && !P.cache_final && k < min(R, pt.n); ++k) early = unit_ref(pt, k).y < pt.n_pages - 1;
+    for (int w = 0; early && !P.cache_final && w < kConsumers; ++w)
+      for (int q = 0; early && q < min(S, units_of(w)); ++q) early = unit_at(w, q).y < pt.n_pages - 1;
     if (early && issuer) produce_range(0, S);
 
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
@@ -816,7 +853,7 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
     // barriers and start again on the new partition.
     if (early && issuer) {
       for (int j = 0; j < S; ++j)
-        if (pcons + kConsumers * j < pt.n && !stage_wait(&full[pcons * S + j], 0)) timed_out = true;
+        if (j < units_of(pcons) && !stage_wait(&full[pcons * S + j], 0)) timed_out = true;
     }
     __syncthreads();
     if (tid == 0) {
@@ -827,7 +864,7 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
       init_barriers();
     }
     early = false;
-    pt = make_part(P, st, c);
+    pt = make_part<kOwner>(P, st, c);
   }
   __syncthreads();  // code tables; barriers reset if the partition changed
   if (!pt.active) {
@@ -838,7 +875,7 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
 
   if (producer) {
     if (issuer) {
-      produce_range(early ? S : 0, (n + kConsumers - 1) / kConsumers);
+      produce_range(early ? S : 0, units_of(pcons));
       if (timed_out) atomicExch(P.ws_error, 1);  // word 0: 1 after a wait ran out
     }
   } else {
@@ -852,6 +889,80 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
     int kvh = 0, gc = gmax;
     // Ring stage and phase of this warp's next unit.
     int js = 0, wrap = 0;
+    // One unit of the ring: wait for its copy, attend, release the stage.
+    auto consume = [&](int page, int half) {
+      const int slot = warp * S + js;
+      const bool ready = stage_wait(&full[slot], uint32_t(wrap) & 1u);
+      if (ready) {
+        const int64_t pos0 = (int64_t(st.first_page) + page) * kPage + half * kHalf;
+        const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, kHalf));
+        // The adapter path takes the radius scale in base-2 units.
+        const float rs = P.int8_radii ? stage_scale[slot] * (kMode == kModeAdapter ? 1.4426950408889634f : 1.f) : 0.f;
+        process_half<kMode, kDenseV>(A, ring + slot * P.stage_bytes, P, lut, tab, qf, rs, vt, lane
+#if TP_QK_CUDA_CORES
+                                     , qcc
+#endif
+        );
+      } else {
+        timed_out = true;  // the unit is left out; the error word marks the result unusable
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (++js == S) { js = 0; ++wrap; }
+    };
+    if (kOwner) {
+      // Whole segments, one after another.  Every consumer warp runs the same segment loop (the
+      // named barriers below count all of them); after a segment the warps' partials are merged
+      // through shared memory into the segment's workspace record while the copy warp keeps
+      // filling the ring with the next segment's units.
+      const int nw = per_segment(warp);
+      constexpr int kCT = kConsumers * 32;  // consumer threads
+      for (int sl = 0; sl < nseg; ++sl) {
+        const int vh = vh_first + sl, chunk = vh % P.nqc;
+        kvh = vh / P.nqc;
+        gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
+        load_q_frags(P, kvh * P.group + chunk * kMaxHeads, gc, lane, qf);
+        acc_reset(A);
+        for (int jj = 0; jj < nw; ++jj) {
+          const int ui = warp + kConsumers * jj;
+          consume(ui >> 1, ui & 1);
+        }
+        if (nw > 0) store_warp_partial<kExactPV>(A, merge + warp * rec_stride, gc, lane);
+        else store_empty_partial(merge + warp * rec_stride, gmax, lane);
+        // The workspace may be the previous call's, whose split combine reads it until it
+        // completes: no record is written before that.
+        if (P.spec && sl == 0) asm volatile("griddepcontrol.wait;\n" ::: "memory");
+        asm volatile("bar.sync 1, %0;\n" ::"n"(kCT) : "memory");
+        for (int i = tid; i < gc * kConsumers; i += kCT) {
+          const int h = i / kConsumers, w = i % kConsumers;
+          const float* recs = merge + h * TP_PARTIAL_FLOATS;
+          float M = recs[0];
+#pragma unroll
+          for (int v = 1; v < kConsumers; ++v) M = fmaxf(M, recs[v * rec_stride]);
+          const float m = recs[w * rec_stride];
+          s_wt[0][h][w] = (m == -INFINITY) ? 0.f : exp2_approx(m - M);
+          if (w == 0) s_wt[0][h][kConsumers] = M;
+        }
+        asm volatile("bar.sync 1, %0;\n" ::"n"(kCT) : "memory");
+        float* rec = P.ws_partials + int64_t(vh) * kPartialStride;
+        for (int i = tid; i < gc * kD; i += kCT) {
+          const int h = i >> 7, d = i & (kD - 1);
+          float L = 0.f, O = 0.f;
+#pragma unroll
+          for (int w = 0; w < kConsumers; ++w) {
+            const float* r = merge + w * rec_stride + h * TP_PARTIAL_FLOATS;
+            const float f = s_wt[0][h][w];
+            L = fmaf(r[1], f, L);
+            O = fmaf(r[2 + d], f, O);
+          }
+          float* out = rec + h * kRecFloats;
+          if (d == 0) { out[0] = s_wt[0][h][kConsumers]; out[1] = L; }
+          out[2 + d] = O;
+        }
+        asm volatile("bar.sync 1, %0;\n" ::"n"(kCT) : "memory");  // merge region and weights free again
+      }
+      if (timed_out && lane == 0) atomicExch(P.ws_error, 1);  // word 0: 1 after a stage-wait timeout
+    } else {
     for (int k = warp; k < n; k += kConsumers) {
       const int3 u = unit_ref(pt, k);
       if (u.x != cur) {
@@ -879,24 +990,7 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
 #endif
         acc_reset(A);
       }
-      const int slot = warp * S + js;
-      const bool ready = stage_wait(&full[slot], uint32_t(wrap) & 1u);
-      if (ready) {
-        const int64_t pos0 = (int64_t(st.first_page) + u.y) * kPage + u.z * kHalf;
-        const int vt = int(clamp64(int64_t(st.seq_len) - pos0, 0, kHalf));
-        // The adapter path takes the radius scale in base-2 units.
-        const float rs = P.int8_radii ? stage_scale[slot] * (kMode == kModeAdapter ? 1.4426950408889634f : 1.f) : 0.f;
-        process_half<kMode, kDenseV>(A, ring + slot * P.stage_bytes, P, lut, tab, qf, rs, vt, lane
-#if TP_QK_CUDA_CORES
-                            , qcc
-#endif
-        );
-      } else {
-        timed_out = true;  // the unit is left out; the error word marks the result unusable
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
-      if (++js == S) { js = 0; ++wrap; }
+      consume(u.y, u.z);
     }
     // Segment 0 partials go to the merge region now; segment 1 partials to this warp's ring
     // stage once every consumer is done with the ring (all issued copies have landed).
@@ -909,9 +1003,11 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
       if (cur == 1) store_warp_partial<kExactPV>(A, rec1, gc, lane);
       else store_empty_partial(rec1, gmax, lane);
     }
+    }
   }
   if (P.spec) asm volatile("griddepcontrol.wait;\n" ::: "memory");
   __syncthreads();
+  if (kOwner) return;  // every segment's record is written
 
   // Merge the warps of each segment and publish this CTA's partial; the split-combine kernel
   // (launched as a programmatic dependent of this grid) merges the CTAs of every head.  The
@@ -1406,7 +1502,10 @@ __global__ void __launch_bounds__(kCombineThreads, 4) split_combine_kernel(const
   // offset of every record to merge: all known before the page pass completes.
   const Grid g = grid_of(P.num_kv_heads * P.nqc, n_pages, P.main_grid);
   int n = 0;
-  if (g.U > 0) {
+  if (P.owner) {
+    n = n_pages > 0 ? 1 : 0;  // one record, merged by the CTA that owns the segment
+    if (tid == 0) soff[0] = vh * kPartialStride + h * kRecFloats;
+  } else if (g.U > 0) {
     const int c_lo = part_owner(g, vh * g.uph);
     n = part_owner(g, vh * g.uph + g.uph - 1) - c_lo + 1;
     for (int ci = tid; ci < n; ci += kCombineThreads) {
@@ -1500,7 +1599,7 @@ __global__ void combine_kernel(const float* partials, int n_parts, int num_q_hea
 // how much of it each page-pass variant has been allowed so far (cudaFuncSetAttribute acts on
 // the current device).
 constexpr int kModes = 3;
-constexpr int kVariants = 2 * kModes;  // key format x (value codes, dense values)
+constexpr int kVariants = 4 * kModes;  // key format x (value codes, dense values) x partition
 constexpr int kMaxDevices = 64;
 struct DeviceCfg {
   int sms = 0;
@@ -1571,14 +1670,30 @@ static cudaError_t reserve_smem(int variant, const void* page_pass, int smem) {
   return e;
 }
 
-// Page-pass CTAs: one per SM, or, with more (KV head, query chunk) segments than SMs (large
-// batches), whole waves of them: every SM then streams the same number of units, and a segment's
-// units span at most three CTAs (the grid is below twice the segment count).
-static int grid_size(int num_kv_heads, int num_q_heads) {
+// (KV head, query chunk) segments of a head layout.
+static int segments_of(int num_kv_heads, int num_q_heads) {
   const int group = num_q_heads / num_kv_heads;
-  const int nqc = (group + kMaxHeads - 1) / kMaxHeads;
-  const int sms = num_sms(), segs = num_kv_heads * nqc;
-  return segs <= sms ? sms : sms * ((segs + sms - 1) / sms);
+  return num_kv_heads * ((group + kMaxHeads - 1) / kMaxHeads);
+}
+
+// Page-pass CTAs.  Up to one segment per SM: one CTA per SM (the flat partition).  With more
+// segments than SMs (large batches), one wave of CTAs that each stream whole segments (the
+// whole-segment partition, AttnParams::owner: the grid is then below the segment count) when
+// the CTAs own nearly equal numbers of segments -- the largest share ceil(V / SMs) at most 1.25x
+// the mean; otherwise whole waves of the flat partition, which stream equal numbers of units
+// (each CTA between half a segment and one, a segment spread over at most three CTAs).
+// Measured on B200 (8 KV heads per sequence, one call): 128 x 512 tokens 55 us whole-segment
+// against 80 in waves, 64 x 1K 44 against 54, 40 x 4K 91 against 80, 19 x 4K 59 against 42.
+static int grid_size(int num_kv_heads, int num_q_heads) {
+  const int sms = num_sms(), segs = segments_of(num_kv_heads, num_q_heads);
+  if (segs <= sms) return sms;
+  const int waves = (segs + sms - 1) / sms;
+  return 4 * waves * sms <= 5 * segs ? sms : waves * sms;
+}
+
+// Workspace record slots: two per CTA (flat partition), or one per segment.
+static int record_slots(int num_kv_heads, int num_q_heads) {
+  return max(2 * grid_size(num_kv_heads, num_q_heads), segments_of(num_kv_heads, num_q_heads));
 }
 
 // float32 (cos, sin) of the decoder angle of a `bits`-bit code, on the host: the angle is
@@ -1630,25 +1745,30 @@ static StreamKey stream_key(cudaStream_t s) {
   return k;
 }
 
-// The page-pass kernels: one per key format, with value codes or dense values.
-template <int kMode, bool kDenseV>
+// The page-pass kernels: one per key format, with value codes or dense values, flat or
+// whole-segment partition.
+template <int kMode, bool kDenseV, bool kOwner>
 static cudaError_t launch_page_pass(const cudaLaunchConfig_t* c, const AttnParams& P) {
-  return cudaLaunchKernelEx(c, decode_attention_kernel<kMode, kDenseV>, P);
+  return cudaLaunchKernelEx(c, decode_attention_kernel<kMode, kDenseV, kOwner>, P);
 }
 struct PagePass {
   const void* fn;
   cudaError_t (*launch)(const cudaLaunchConfig_t*, const AttnParams&);
 };
-template <int kMode, bool kDenseV>
+template <int kMode, bool kDenseV, bool kOwner>
 static PagePass page_pass_of() {
-  return {reinterpret_cast<const void*>(decode_attention_kernel<kMode, kDenseV>), launch_page_pass<kMode, kDenseV>};
+  return {reinterpret_cast<const void*>(decode_attention_kernel<kMode, kDenseV, kOwner>),
+          launch_page_pass<kMode, kDenseV, kOwner>};
 }
-static PagePass page_pass(int mode, bool dense_v) {
-  if (dense_v)
-    return mode == kModeFast ? page_pass_of<kModeFast, true>()
-           : mode == kModeAdapter ? page_pass_of<kModeAdapter, true>() : page_pass_of<kModeGeneral, true>();
-  return mode == kModeFast ? page_pass_of<kModeFast, false>()
-         : mode == kModeAdapter ? page_pass_of<kModeAdapter, false>() : page_pass_of<kModeGeneral, false>();
+template <bool kDenseV, bool kOwner>
+static PagePass page_pass_for(int mode) {
+  return mode == kModeFast      ? page_pass_of<kModeFast, kDenseV, kOwner>()
+         : mode == kModeAdapter ? page_pass_of<kModeAdapter, kDenseV, kOwner>()
+                                : page_pass_of<kModeGeneral, kDenseV, kOwner>();
+}
+static PagePass page_pass(int mode, bool dense_v, bool owner) {
+  if (dense_v) return owner ? page_pass_for<true, true>(mode) : page_pass_for<true, false>(mode);
+  return owner ? page_pass_for<false, true>(mode) : page_pass_for<false, false>(mode);
 }
 
 // cuTensorMapEncodeTiled from the driver (resolved once; NULL when the driver lacks it).
@@ -1693,8 +1813,7 @@ extern "C" {
 
 size_t tp_decode_attention_workspace_size(int32_t num_kv_heads, int32_t num_q_heads) {
   if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads) return 0;
-  const int grid = grid_size(num_kv_heads, num_q_heads);
-  const size_t bytes = 256 + size_t(grid) * 2 * kPartialStride * sizeof(float);
+  const size_t bytes = 256 + size_t(record_slots(num_kv_heads, num_q_heads)) * kPartialStride * sizeof(float);
   return (bytes + 255) & ~size_t(255);
 }
 
@@ -1769,8 +1888,9 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
   P.partial_out = partial_out;
   const int grid = grid_size(hkv, num_q_heads);
   P.main_grid = grid;
-  // CTAs sharing one segment: up to the grid when it is one wave (no more segments than SMs),
-  // at most three beyond (each CTA then holds between half a segment and one segment).
+  P.owner = hkv * P.nqc > grid ? 1 : 0;
+  // CTAs sharing one segment: up to the grid with one wave of the flat partition, at most three
+  // with more waves, one with the whole-segment partition.
   if (hkv * P.nqc <= num_sms() && grid > kMaxContrib)
     return fail(TP_ERR_UNSUPPORTED, "tp_decode_attention: more SMs than one head's partials can merge");
   P.ws_error = static_cast<int*>(workspace);  // word 0: error
@@ -1829,9 +1949,9 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
 
   fill_decoder_table(mode, P.cs);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const PagePass pass = page_pass(mode, dv != nullptr);
+  const PagePass pass = page_pass(mode, dv != nullptr, P.owner != 0);
   const void* fn = pass.fn;
-  const int variant = mode + (dv ? kModes : 0);
+  const int variant = mode + (dv ? kModes : 0) + (P.owner ? 2 * kModes : 0);
   // Ring stages: as many as fit while a split-combine CTA still fits beside the page-pass CTA
   // on one SM (so it starts, and finishes the dense tail, while the page pass runs); with dense
   // values 1024 bytes go to aligning the ring, and one stage per compute warp is accepted.  A
