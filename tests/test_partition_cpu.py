@@ -9,8 +9,8 @@ rely on.
 * More segments than SMs (large batches), when the CTAs own nearly equal numbers of segments
   (the largest share at most 1.25x the mean): the whole-segment partition, one CTA per SM owning
   the segments [floor(c*V/G), floor((c+1)*V/G)); every segment has exactly one owner (its one
-  record is the segment's merged partial) and every CTA owns at least one.  Inside a CTA, warp
-  w streams units w, w + 7, ... of each segment in turn.
+  records are its CTA's compute warps' partials) and every CTA owns at least one.  Inside a CTA,
+  warp w streams units w, w + 7, ... of the CTA's segments laid end to end.
 * Otherwise, whole waves of the flat partition: every CTA holds between half a segment and one,
   a segment spreads over at most three CTAs.
 """
@@ -95,18 +95,21 @@ def test_whole_segment_partition_bounds():
         assert max(sizes) - min(sizes) <= 1
 
 
-def test_whole_segment_unit_order_covers_every_unit_once():
-    """The copy warp's q-th unit for warp w (unit_at) and the compute warp's loop agree, and the
-    warps together take every unit of every owned segment once."""
+def test_whole_segment_unit_order_and_records():
+    """Warp w takes CTA units w, w + 7, ... of the CTA's segments laid end to end (unit_at and the
+    compute warp's loop); together the warps take every unit once, and each warp's units of one
+    segment are consecutive in its order, so it leaves one record per segment (empty for a
+    segment it has no unit of)."""
     for n_pages in (1, 2, 3, 4, 9, 64):
         uph = 2 * n_pages
         for nseg in (1, 2, 7):
+            n = nseg * uph
             seen = set()
             for w in range(CONSUMERS):
-                nw = (uph - 1 - w) // CONSUMERS + 1 if w < uph else 0
-                loop = [(sl, w + CONSUMERS * jj) for sl in range(nseg) for jj in range(nw)]
-                for q, (sl, ui) in enumerate(loop):
-                    seg = q // nw
-                    assert (seg, w + CONSUMERS * (q - seg * nw)) == (sl, ui)
-                    seen.add((sl, ui))
-            assert seen == {(s, u) for s in range(nseg) for u in range(uph)}
+                units = [(k // uph, k % uph) for k in range(w, n, CONSUMERS)]
+                nu = (n - 1 - w) // CONSUMERS + 1 if n > w else 0
+                assert len(units) == nu
+                segs = [sl for sl, _ in units]
+                assert segs == sorted(segs)  # one run per segment
+                seen.update(units)
+            assert seen == {(sl, j) for sl in range(nseg) for j in range(uph)}

@@ -593,8 +593,9 @@ __device__ __forceinline__ void load_q_frags(const AttnParams& P, int qh_base, i
   }
 }
 
-// Write this warp's partial (m, l, o) for the heads < gc to a [gc][130] record.
-template <bool kExact>
+// Write this warp's partial (m, l, o) for the heads < gc to a record of kHeadStride floats a
+// head ([gc][130] in shared memory; [gc][132] in the workspace, 16-byte aligned heads).
+template <bool kExact, int kHeadStride = TP_PARTIAL_FLOATS>
 __device__ __forceinline__ void store_warp_partial(WarpAcc& A, float* rec, int gc, int lane) {
   const int g = lane >> 2, t = lane & 3;
   float l0 = A.l[0], l1 = A.l[1];
@@ -610,22 +611,23 @@ __device__ __forceinline__ void store_warp_partial(WarpAcc& A, float* rec, int g
     const int d = 32 * G + 4 * g + 2 * (md & 1);
     const float c0 = kExact ? 0.f : 1152.f * A.ones[G][0], c1 = kExact ? 0.f : 1152.f * A.ones[G][1];
     if (h0 < gc) {
-      rec[h0 * TP_PARTIAL_FLOATS + 2 + d] = A.o[md][0] - c0;
-      rec[h0 * TP_PARTIAL_FLOATS + 3 + d] = A.o[md][2] - c0;
+      rec[h0 * kHeadStride + 2 + d] = A.o[md][0] - c0;
+      rec[h0 * kHeadStride + 3 + d] = A.o[md][2] - c0;
     }
     if (h1 < gc) {
-      rec[h1 * TP_PARTIAL_FLOATS + 2 + d] = A.o[md][1] - c1;
-      rec[h1 * TP_PARTIAL_FLOATS + 3 + d] = A.o[md][3] - c1;
+      rec[h1 * kHeadStride + 2 + d] = A.o[md][1] - c1;
+      rec[h1 * kHeadStride + 3 + d] = A.o[md][3] - c1;
     }
   }
   if (g == 0) {
-    if (h0 < gc) { rec[h0 * TP_PARTIAL_FLOATS] = A.m[0]; rec[h0 * TP_PARTIAL_FLOATS + 1] = l0; }
-    if (h1 < gc) { rec[h1 * TP_PARTIAL_FLOATS] = A.m[1]; rec[h1 * TP_PARTIAL_FLOATS + 1] = l1; }
+    if (h0 < gc) { rec[h0 * kHeadStride] = A.m[0]; rec[h0 * kHeadStride + 1] = l0; }
+    if (h1 < gc) { rec[h1 * kHeadStride] = A.m[1]; rec[h1 * kHeadStride + 1] = l1; }
   }
 }
 
+template <int kHeadStride = TP_PARTIAL_FLOATS>
 __device__ __forceinline__ void store_empty_partial(float* rec, int gc, int lane) {
-  for (int i = lane; i < gc * TP_PARTIAL_FLOATS; i += 32) rec[i] = (i % TP_PARTIAL_FLOATS == 0) ? -INFINITY : 0.f;
+  for (int i = lane; i < gc * kHeadStride; i += 32) rec[i] = (i % kHeadStride == 0) ? -INFINITY : 0.f;
 }
 
 // Final write of one head's merged (m, l, o[d]).
@@ -785,18 +787,14 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
   __syncthreads();  // barriers initialised and the state read before any producer issues
   Part pt = make_part<kOwner>(P, s_pre, c);
   bool timed_out = false;
-  // Units of consumer w, and its q-th unit as (segment, page, half).  The flat partition deals
-  // CTA units w, w + kConsumers, ...; the whole-segment partition deals each segment's units
-  // w, w + kConsumers, ... < 2 * n_pages, segment after segment.
-  auto per_segment = [&](int w) { return w < 2 * pt.n_pages ? (2 * pt.n_pages - 1 - w) / kConsumers + 1 : 0; };
-  auto units_of = [&](int w) {
-    if (kOwner) return pt.nseg * per_segment(w);
-    return pt.n > w ? (pt.n - 1 - w) / kConsumers + 1 : 0;
-  };
+  // Units of consumer w, and its q-th unit as (segment, page, half): CTA units w, w + kConsumers,
+  // ... of the CTA's unit list (the whole-segment partition's list runs through its segments one
+  // after another).
+  auto units_of = [&](int w) { return pt.n > w ? (pt.n - 1 - w) / kConsumers + 1 : 0; };
   auto unit_at = [&](int w, int q) {
     if (kOwner) {
-      const int nw = per_segment(w), seg = q / nw, ui = w + kConsumers * (q - seg * nw);
-      return make_int3(seg, ui >> 1, ui & 1);
+      const int k = w + kConsumers * q, uph = 2 * pt.n_pages, seg = k / uph, j = k - seg * uph;
+      return make_int3(seg, j >> 1, j & 1);
     }
     return unit_ref(pt, w + kConsumers * q);
   };
@@ -911,56 +909,41 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
       if (++js == S) { js = 0; ++wrap; }
     };
     if (kOwner) {
-      // Whole segments, one after another.  Every consumer warp runs the same segment loop (the
-      // named barriers below count all of them); after a segment the warps' partials are merged
-      // through shared memory into the segment's workspace record while the copy warp keeps
-      // filling the ring with the next segment's units.
-      const int nw = per_segment(warp);
-      constexpr int kCT = kConsumers * 32;  // consumer threads
-      for (int sl = 0; sl < nseg; ++sl) {
-        const int vh = vh_first + sl, chunk = vh % P.nqc;
-        kvh = vh / P.nqc;
-        gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
-        load_q_frags(P, kvh * P.group + chunk * kMaxHeads, gc, lane, qf);
-        acc_reset(A);
-        for (int jj = 0; jj < nw; ++jj) {
-          const int ui = warp + kConsumers * jj;
-          consume(ui >> 1, ui & 1);
+      // Whole segments.  The warp's units run through the CTA's segments one after another; at
+      // every change of segment it writes its partial of the segment it leaves to that segment's
+      // workspace record of this warp, (segment * kConsumers + warp), and an empty record for
+      // every segment it has no unit of, so the split combine finds kConsumers records per
+      // segment.  Nothing here waits for the other warps.
+      const int uph = 2 * pt.n_pages;
+      bool waited = !P.spec;  // the workspace may be the previous call's (see below)
+      auto rec_of = [&](int sl) {
+        return P.ws_partials + (int64_t(vh_first + sl) * kConsumers + warp) * kPartialStride;
+      };
+      auto before_store = [&]() {
+        if (!waited) {  // the previous call's split combine reads its records until it completes
+          asm volatile("griddepcontrol.wait;\n" ::: "memory");
+          waited = true;
         }
-        if (nw > 0) store_warp_partial<kExactPV>(A, merge + warp * rec_stride, gc, lane);
-        else store_empty_partial(merge + warp * rec_stride, gmax, lane);
-        // The workspace may be the previous call's, whose split combine reads it until it
-        // completes: no record is written before that.
-        if (P.spec && sl == 0) asm volatile("griddepcontrol.wait;\n" ::: "memory");
-        asm volatile("bar.sync 1, %0;\n" ::"n"(kCT) : "memory");
-        for (int i = tid; i < gc * kConsumers; i += kCT) {
-          const int h = i / kConsumers, w = i % kConsumers;
-          const float* recs = merge + h * TP_PARTIAL_FLOATS;
-          float M = recs[0];
-#pragma unroll
-          for (int v = 1; v < kConsumers; ++v) M = fmaxf(M, recs[v * rec_stride]);
-          const float m = recs[w * rec_stride];
-          s_wt[0][h][w] = (m == -INFINITY) ? 0.f : exp2_approx(m - M);
-          if (w == 0) s_wt[0][h][kConsumers] = M;
+      };
+      cur = -1;
+      for (int k = warp; k < n; k += kConsumers) {
+        const int sl = k / uph, j = k - sl * uph;
+        if (sl != cur) {
+          before_store();
+          if (cur >= 0) store_warp_partial<kExactPV, kRecFloats>(A, rec_of(cur), gc, lane);
+          for (int e = cur + 1; e < sl; ++e) store_empty_partial<kRecFloats>(rec_of(e), gmax, lane);
+          cur = sl;
+          const int vh = vh_first + sl, chunk = vh % P.nqc;
+          kvh = vh / P.nqc;
+          gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
+          load_q_frags(P, kvh * P.group + chunk * kMaxHeads, gc, lane, qf);
+          acc_reset(A);
         }
-        asm volatile("bar.sync 1, %0;\n" ::"n"(kCT) : "memory");
-        float* rec = P.ws_partials + int64_t(vh) * kPartialStride;
-        for (int i = tid; i < gc * kD; i += kCT) {
-          const int h = i >> 7, d = i & (kD - 1);
-          float L = 0.f, O = 0.f;
-#pragma unroll
-          for (int w = 0; w < kConsumers; ++w) {
-            const float* r = merge + w * rec_stride + h * TP_PARTIAL_FLOATS;
-            const float f = s_wt[0][h][w];
-            L = fmaf(r[1], f, L);
-            O = fmaf(r[2 + d], f, O);
-          }
-          float* out = rec + h * kRecFloats;
-          if (d == 0) { out[0] = s_wt[0][h][kConsumers]; out[1] = L; }
-          out[2 + d] = O;
-        }
-        asm volatile("bar.sync 1, %0;\n" ::"n"(kCT) : "memory");  // merge region and weights free again
+        consume(j >> 1, j & 1);
       }
+      before_store();
+      if (cur >= 0) store_warp_partial<kExactPV, kRecFloats>(A, rec_of(cur), gc, lane);
+      for (int e = cur + 1; e < nseg; ++e) store_empty_partial<kRecFloats>(rec_of(e), gmax, lane);
       if (timed_out && lane == 0) atomicExch(P.ws_error, 1);  // word 0: 1 after a stage-wait timeout
     } else {
     for (int k = warp; k < n; k += kConsumers) {
@@ -1503,8 +1486,8 @@ __global__ void __launch_bounds__(kCombineThreads, 4) split_combine_kernel(const
   const Grid g = grid_of(P.num_kv_heads * P.nqc, n_pages, P.main_grid);
   int n = 0;
   if (P.owner) {
-    n = n_pages > 0 ? 1 : 0;  // one record, merged by the CTA that owns the segment
-    if (tid == 0) soff[0] = vh * kPartialStride + h * kRecFloats;
+    n = n_pages > 0 ? kConsumers : 0;  // the owning CTA's warps' records of this segment
+    if (tid < n) soff[tid] = (vh * kConsumers + tid) * kPartialStride + h * kRecFloats;
   } else if (g.U > 0) {
     const int c_lo = part_owner(g, vh * g.uph);
     n = part_owner(g, vh * g.uph + g.uph - 1) - c_lo + 1;
@@ -1691,9 +1674,11 @@ static int grid_size(int num_kv_heads, int num_q_heads) {
   return 4 * waves * sms <= 5 * segs ? sms : waves * sms;
 }
 
-// Workspace record slots: two per CTA (flat partition), or one per segment.
+// Workspace record slots: two per CTA (flat partition), or one per segment and compute warp
+// (whole-segment partition).
 static int record_slots(int num_kv_heads, int num_q_heads) {
-  return max(2 * grid_size(num_kv_heads, num_q_heads), segments_of(num_kv_heads, num_q_heads));
+  const int grid = grid_size(num_kv_heads, num_q_heads), segs = segments_of(num_kv_heads, num_q_heads);
+  return segs > grid ? segs * kConsumers : 2 * grid;
 }
 
 // float32 (cos, sin) of the decoder angle of a `bits`-bit code, on the host: the angle is
