@@ -8,7 +8,8 @@ device time comes from CUDA events around the replays on the launching stream.  
 time and the achieved GB/s of algorithmic bytes (compressed pages + dense tail + q + out), for
 independent launches (every layer reads the same query) and for a dependent chain (each
 layer's query is the previous layer's output).
-``--launches N`` instead issues N plain launches over the layers (for ncu: one kernel per
+``--batch B`` times calls over B sequences each (B x H_kv flattened KV heads).  ``--launches N``
+instead issues N plain launches over the layers (for ncu: one kernel per
 launch, no graph).  ``--dense-v`` times tp_decode_attention_dense_v instead (the keys of the
 same pages, float16 values from a separate array; no dense tail: ``--ctx`` a multiple of 64).
 """
@@ -35,22 +36,22 @@ L2_BYTES = 126 * 2 ** 20
 
 def make_layers(a, dev):
     cfg = TurboPolarConfig(num_q_heads=a.hq, num_kv_heads=a.hkv, **FORMATS[a.format])
-    per_layer = (a.ctx // 64) * a.hkv * page_bytes(cfg.format_fields()) + (a.ctx * a.hkv * 256 if a.dense_v else 0)
+    per_layer = a.batch * ((a.ctx // 64) * a.hkv * page_bytes(cfg.format_fields()) + (a.ctx * a.hkv * 256 if a.dense_v else 0))
     n = a.layers or max(1, math.ceil(4 * L2_BYTES / max(per_layer, 1)))
     gen = torch.Generator(device=dev)
     chan = torch.from_numpy(np.random.default_rng(1).uniform(0.5, 4.0, size=128).astype(np.float32)).to(dev)
     layers, values = [], []
     for i in range(n):
         gen.manual_seed(a.seed + i)
-        k = (torch.randn((1, a.hkv, a.ctx, 128), generator=gen, device=dev) * chan).half()
-        v = torch.randn((1, a.hkv, a.ctx, 128), generator=gen, device=dev).half()
+        k = (torch.randn((a.batch, a.hkv, a.ctx, 128), generator=gen, device=dev) * chan).half()
+        v = torch.randn((a.batch, a.hkv, a.ctx, 128), generator=gen, device=dev).half()
         rt = TurboPolarKVCacheRuntime(cfg, max_seq_len=a.ctx, check_finite=False)
         rt.append(k, v)
         if a.dense_v:
-            values.append(v[0].contiguous())
+            values.append(v.reshape(a.batch * a.hkv, a.ctx, 128).contiguous())
         del k, v
         layers.append(rt)
-    q = torch.randn((1, a.hq, 128), generator=gen, device=dev).half()
+    q = torch.randn((a.batch, a.hq, 128), generator=gen, device=dev).half()
     return cfg, layers, values, q
 
 
@@ -59,7 +60,8 @@ def dense_v_caller(a, layers, values, dev):
     if a.ctx % 64:
         raise SystemExit("--dense-v needs --ctx a multiple of 64")
     lib = _lib.lib()
-    ws = [torch.zeros(lib.tp_decode_attention_workspace_size(a.hkv, a.hq), dtype=torch.uint8, device=dev)
+    heads, q_heads = a.batch * a.hkv, a.batch * a.hq
+    ws = [torch.zeros(lib.tp_decode_attention_workspace_size(heads, q_heads), dtype=torch.uint8, device=dev)
           for _ in layers]
     scale = float(layers[0].config.attention_scale)
 
@@ -67,7 +69,7 @@ def dense_v_caller(a, layers, values, dev):
         rt = layers[i]
         _lib.check(lib.tp_decode_attention_dense_v(
             ctypes.byref(rt.pool_struct()), _lib.State(rt.n_pages, 0, a.ctx, 0), values[i].data_ptr(), a.ctx * 128,
-            a.ctx, q.data_ptr(), _lib.TP_F16, a.hq, scale, out.data_ptr(), None, ws[i].data_ptr(), ws[i].numel(),
+            a.ctx, q.data_ptr(), _lib.TP_F16, q_heads, scale, out.data_ptr(), None, ws[i].data_ptr(), ws[i].numel(),
             torch.cuda.current_stream(dev).cuda_stream))
     return attend
 
@@ -77,6 +79,7 @@ def main(argv=None):
     ap.add_argument("--ctx", type=int, default=32768)
     ap.add_argument("--hq", type=int, default=32)
     ap.add_argument("--hkv", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=1, help="sequences per call (KV heads flattened batch-major)")
     ap.add_argument("--layers", type=int, default=0, help="0: enough layers to exceed 4x L2")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--launches", type=int, default=0, help="plain launches instead of graph replays")
@@ -87,7 +90,7 @@ def main(argv=None):
     build.build()
     dev = torch.device("cuda:0")
     cfg, layers, values, q = make_layers(a, dev)
-    outs = [torch.empty((1, a.hq, 128), dtype=torch.float16, device=dev) for _ in layers]
+    outs = [torch.empty((a.batch, a.hq, 128), dtype=torch.float16, device=dev) for _ in layers]
     if a.dense_v:
         attend = dense_v_caller(a, layers, values, dev)
     else:
@@ -101,9 +104,9 @@ def main(argv=None):
         fmt = rt0.fmt
         l1, deep = row_bytes(fmt)
         k_row = (64 if fmt["int8_radii"] else 128) + l1 + deep
-        nbytes = rt0.n_pages * 64 * a.hkv * (k_row + 256) + a.hq * 128 * 4
+        nbytes = a.batch * (rt0.n_pages * 64 * a.hkv * (k_row + 256) + a.hq * 128 * 4)
     else:
-        nbytes = rt0.n_pages * a.hkv * page_bytes(rt0.fmt) + rt0.tail_len * a.hkv * 128 * 4 + a.hq * 128 * 4
+        nbytes = a.batch * (rt0.n_pages * a.hkv * page_bytes(rt0.fmt) + rt0.tail_len * a.hkv * 128 * 4 + a.hq * 128 * 4)
     if a.launches:
         for i in range(a.launches):
             attend(i % len(layers), q, outs[i % len(layers)])
@@ -133,7 +136,7 @@ def main(argv=None):
     # one has completed).
     us = per_launch_us(False)
     dep = per_launch_us(True)
-    print(json.dumps({"ctx": a.ctx, "hq": a.hq, "hkv": a.hkv, "format": a.format, "dense_v": a.dense_v,
+    print(json.dumps({"ctx": a.ctx, "batch": a.batch, "hq": a.hq, "hkv": a.hkv, "format": a.format, "dense_v": a.dense_v,
                       "layers": len(layers),
                       "us_per_launch": us, "bytes_per_launch": nbytes, "gbs": nbytes / us / 1e3,
                       "us_per_launch_dependent": dep, "gbs_dependent": nbytes / dep / 1e3}))
