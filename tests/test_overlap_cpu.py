@@ -53,6 +53,18 @@ static bool run_probe(StreamLog& log, const void* stream, const CallBuffers& b, 
   return log.independent(StreamKey{0, uintptr_t(stream), 0, 0}, r, w, &c, cache_final);
 }
 
+// The decision and whether the call's workspace at `ws` is used by no call of the chain.
+static bool run_ws(StreamLog& log, const void* stream, CallBuffers b, size_t ws, bool* ws_clear) {
+  b.workspace = at(ws);
+  b.workspace_bytes = 4096;
+  Spans r, w, c, x;
+  call_spans(b, r, w);
+  cache_spans(b, c);
+  workspace_spans(b, x);
+  bool fin = false;
+  return log.independent(StreamKey{0, uintptr_t(stream), 0, 0}, r, w, &c, &fin, &x, ws_clear);
+}
+
 #define CHECK(cond) do { if (!(cond)) { std::printf("FAIL line %d: %s\n", __LINE__, #cond); std::exit(1); } } while (0)
 
 int main() {
@@ -184,6 +196,26 @@ int main() {
     // and the step (still running, perhaps) writes the cache.
     run_probe(log, s1, call(200000, 300000, 440000, true), &fin);
     CHECK(!run_probe(log, s1, call(200000, 440000, 450000, false), &fin) && !fin);
+  }
+  {  // workspaces: a call may write its partials before its wait only when it is independent
+     // and no call of the chain (back to the last one that waited) uses an overlapping workspace
+    StreamLog log;
+    bool clear = true;
+    CHECK(!run_ws(log, s1, call(0, 300000, 400000, true), 800000, &clear) && !clear);   // first call
+    CHECK(run_ws(log, s1, call(100000, 310000, 410000, true), 810000, &clear) && clear);  // own workspace
+    CHECK(run_ws(log, s1, call(200000, 320000, 420000, true), 820000, &clear) && clear);
+    // Another layer sharing the first layer's workspace: independent, but that workspace's
+    // partials may still be read by the first call's split combine.
+    CHECK(run_ws(log, s1, call(300000, 330000, 430000, true), 800000 + 4095, &clear) && !clear);
+    // Adjacent to the second layer's workspace, not overlapping it.
+    CHECK(run_ws(log, s1, call(500000, 640000, 440000, true), 810000 + 4096, &clear) && clear);
+    // A dependent call (same cache as the second layer) waits first: never "clear", and the chain
+    // of workspaces restarts with its own.
+    CHECK(!run_ws(log, s1, call(100000, 350000, 450000, true), 830000, &clear) && !clear);
+    CHECK(run_ws(log, s1, call(0, 360000, 460000, true), 800000, &clear) && clear);  // the old chain is done
+    CHECK(run_ws(log, s1, call(200000, 370000, 470000, true), 830000, &clear) && !clear);
+    // No workspace given: never clear.
+    CHECK(run(log, s1, call(300000, 380000, 480000, false)));
   }
   {  // more ranges than fit count as overlapping everything
     Spans r, w;

@@ -107,6 +107,9 @@ struct AttnParams {
   // The previous call launched on this stream writes nothing this call reads: the page pass
   // streams before griddepcontrol.wait (the host decides: StreamLog in tp_overlap.h).
   int spec;
+  // With spec: no call that may still be running uses this call's workspace, so the page pass
+  // writes its partials first and waits for the previous kernel only before it exits.
+  int ws_private;
   // No call that may still be running writes this call's state words, pages or radius scales:
   // what the page pass reads of them before griddepcontrol.wait is final (StreamLog's probe).
   int cache_final;
@@ -867,6 +870,9 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
   __syncthreads();  // code tables; barriers reset if the partition changed
   if (!pt.active) {
     if (timed_out) atomicExch(P.ws_error, 1);
+    // The grid's completion must imply the previous kernel's (a later call that waits for this
+    // call relies on it), also when no CTA has a unit.
+    if (P.spec) asm volatile("griddepcontrol.wait;\n" ::: "memory");
     return;
   }
   const int n = pt.n, nseg = pt.nseg, vh_first = pt.vh_first;
@@ -915,7 +921,7 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
       // every segment it has no unit of, so the split combine finds kConsumers records per
       // segment.  Nothing here waits for the other warps.
       const int uph = 2 * pt.n_pages;
-      bool waited = !P.spec;  // the workspace may be the previous call's (see below)
+      bool waited = !P.spec || P.ws_private;  // the workspace may be the previous call's (see below)
       auto rec_of = [&](int sl) {
         return P.ws_partials + (int64_t(vh_first + sl) * kConsumers + warp) * kPartialStride;
       };
@@ -988,9 +994,12 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
     }
     }
   }
-  if (P.spec) asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  if (P.spec && !P.ws_private) asm volatile("griddepcontrol.wait;\n" ::: "memory");
   __syncthreads();
-  if (kOwner) return;  // every segment's record is written
+  if (kOwner) {  // every segment's record is written
+    if (P.spec && P.ws_private) asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    return;
+  }
 
   // Merge the warps of each segment and publish this CTA's partial; the split-combine kernel
   // (launched as a programmatic dependent of this grid) merges the CTAs of every head.  The
@@ -1033,6 +1042,9 @@ __global__ void __maxnreg__(TP_PAGE_PASS_REGS) decode_attention_kernel(const __g
       out[2 + d] = O;
     }
   }
+  // Private workspace: the partials are written; the grid completes only after the previous
+  // kernel in the stream has.
+  if (P.spec && P.ws_private) asm volatile("griddepcontrol.wait;\n" ::: "memory");
 }
 
 // Merge the per-CTA partials of one query head -- from the CTAs whose unit ranges cover its
@@ -1996,8 +2008,14 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
     call_spans(b, reads, writes);
     cache_spans(b, cache);
     bool cache_final = false;
-    P.spec = g_stream_log.independent(stream_key(s), reads, writes, &cache, &cache_final) ? 1 : 0;
+    b.workspace = workspace;
+    b.workspace_bytes = need;
+    Spans ws;
+    workspace_spans(b, ws);
+    bool ws_clear = false;
+    P.spec = g_stream_log.independent(stream_key(s), reads, writes, &cache, &cache_final, &ws, &ws_clear) ? 1 : 0;
     P.cache_final = cache_final ? 1 : 0;
+    P.ws_private = ws_clear ? 1 : 0;
   }
   // The page pass is a programmatic dependent of whatever precedes it in the stream (a no-op
   // unless that kernel triggers early, as the split combine of a previous call does): its

@@ -62,7 +62,12 @@ struct CallBuffers {
   size_t exchange_bytes = 0;
   const void* values = nullptr;        // dense value array (dense-V call), read
   size_t values_bytes = 0;
+  const void* workspace = nullptr;     // partials and error word, written (see StreamLog)
+  size_t workspace_bytes = 0;
 };
+
+// The workspace of `b`.
+inline void workspace_spans(const CallBuffers& b, Spans& out) { out.add(b.workspace, b.workspace_bytes); }
 
 // The cache a page pass reads before griddepcontrol.wait: state words, pages, radius scales.
 inline void cache_spans(const CallBuffers& b, Spans& out) {
@@ -71,8 +76,9 @@ inline void cache_spans(const CallBuffers& b, Spans& out) {
   out.add(b.radii_scales, b.radii_scales_bytes);
 }
 
-// What `b` reads and writes.  The workspace is left out of both sides: the page pass writes its
-// partials only after griddepcontrol.wait, and the split combine reads them after its own.  A
+// What `b` reads and writes.  The workspace is left out of both sides (StreamLog tracks it on
+// its own): the page pass writes its partials only after griddepcontrol.wait unless no call
+// that may still run uses the same workspace, and the split combine reads them after its own.  A
 // sharded call's split combine reads and advances the epoch in this rank's exchange buffer
 // before its wait, so the buffer counts as read and written and two calls on one exchange
 // never overlap (calls on different exchanges, one per layer, may); the other ranks' buffers
@@ -158,17 +164,29 @@ struct ChainWrites {
   }
 };
 
+// The chain of one stream: its calls' writes and, apart, their workspaces.
+struct Chain {
+  ChainWrites writes, ws;
+};
+
 class StreamLog {
  public:
   // True when this call may read early: the stream has a chain and nothing its calls write is
   // read by this call.  Adds this call's writes to the chain, or restarts the chain with them.
   // With `probe`, *probe_clear tells whether the chain (before this call) writes none of the
   // probe's ranges: what a dependent call reads of them before its wait is then final too.
+  // With `ws` (this call's workspace), *ws_clear tells whether the call is independent and no
+  // call of the chain uses an overlapping workspace: its page pass may then write its partials
+  // before it waits for the previous call (it still waits before it completes, so that its
+  // completion implies the previous call's).  The chain keeps the workspaces beside the writes.
   bool independent(const StreamKey& key, const Spans& reads, const Spans& writes, const Spans* probe = nullptr,
-                   bool* probe_clear = nullptr) {
+                   bool* probe_clear = nullptr, const Spans* ws = nullptr, bool* ws_clear = nullptr) {
     std::lock_guard<std::mutex> lock(mu_);
+    const Spans none{};
+    const Spans& w = ws ? *ws : none;
     auto it = last_.find(key);
-    if (probe_clear) *probe_clear = it != last_.end() && !it->second.meets(*probe);
+    if (probe_clear) *probe_clear = it != last_.end() && !it->second.writes.meets(*probe);
+    if (ws_clear) *ws_clear = false;
     if (it == last_.end()) {
       if (key.capture != 0) {
         for (auto j = last_.begin(); j != last_.end();) {
@@ -179,12 +197,21 @@ class StreamLog {
             ++j;
         }
       }
-      last_[key].reset(writes);
+      Chain& c = last_[key];
+      c.writes.reset(writes);
+      c.ws.reset(w);
       return false;
     }
-    const bool ok = !it->second.meets(reads);
-    if (ok) it->second.add(writes);
-    else it->second.reset(writes);
+    Chain& c = it->second;
+    const bool ok = !c.writes.meets(reads);
+    if (ok) {
+      if (ws_clear) *ws_clear = !w.all && w.n > 0 && !c.ws.meets(w);
+      c.writes.add(writes);
+      c.ws.add(w);
+    } else {
+      c.writes.reset(writes);
+      c.ws.reset(w);
+    }
     return ok;
   }
   size_t size() {
@@ -194,7 +221,7 @@ class StreamLog {
 
  private:
   std::mutex mu_;
-  std::map<StreamKey, ChainWrites> last_;
+  std::map<StreamKey, Chain> last_;
 };
 
 }  // namespace tp
