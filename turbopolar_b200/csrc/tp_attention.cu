@@ -1403,7 +1403,7 @@ __device__ __forceinline__ void advance_state(const AttnParams& P, const tp_stat
 }
 
 // At most 64 registers a thread, so a split-combine CTA fits beside a page-pass CTA (177).
-__global__ void __launch_bounds__(kCombineThreads, 4) split_combine_kernel(const __grid_constant__ AttnParams P) {
+__global__ void __launch_bounds__(kCombineThreads, 5) split_combine_kernel(const __grid_constant__ AttnParams P) {
   __shared__ __align__(16) CombineSmem sm;
   __shared__ int soff[kMaxContrib];
   __shared__ __align__(16) float s_o[kCombineWarps * kD];
@@ -1571,6 +1571,140 @@ __global__ void __launch_bounds__(kCombineThreads, 4) split_combine_kernel(const
   if (s_last && tid == 0) advance_state(P, st, n_pages, tail_len, appended, flush);
 }
 
+// Plain attention (no decode step, no exchange) over more (KV head, query chunk) segments than
+// SMs, as a batch of sequences gives: one CTA per segment merges all gc query heads of the
+// segment, instead of one CTA per query head.  A workspace record holds the partials of every
+// head of its segment side by side, so one round of copies stages the records of all heads;
+// the heads' dense-tail partials run one after another before griddepcontrol.wait.  Per head
+// the arithmetic is split_combine_kernel's: the tail partial opens half 0, the records of even
+// and odd position merge in the two halves chunk by chunk (max, rescale, accumulate), and the
+// halves combine at the end.  A segment has at most 7 records here (whole-segment partition:
+// one per compute warp; whole waves: at most three CTAs), so one chunk holds them all.  Launched as a programmatic dependent of the
+// page pass like split_combine_kernel; its static shared memory is no larger, so a CTA fits
+// beside a page-pass CTA.
+constexpr int kSegRecs = 56;  // records of the staging area in one chunk (the rest: tail partials)
+__global__ void __launch_bounds__(kCombineThreads, 4) segment_combine_kernel(const __grid_constant__ AttnParams P) {
+  __shared__ __align__(16) float recs[kCombineChunk * kRecFloats];
+  __shared__ int soff[kMaxContrib];
+  __shared__ __align__(16) float s_o[kCombineWarps * kD];
+  __shared__ float s_sc[kPage + kCombineWarps];
+  __shared__ float s_tm[kMaxHeads][2];
+  __shared__ tp_state s_st;
+  float* s_to = recs + kSegRecs * kRecFloats;  // tail partials o[h][128], until the records land
+  static_assert((kCombineChunk - kSegRecs) * kRecFloats >= kMaxHeads * kD, "tail partials");
+  const int tid = threadIdx.x;
+  const int vh = blockIdx.x;
+  const int kvh = vh / P.nqc, chunk = vh % P.nqc;
+  const int gc = min(kMaxHeads, P.group - chunk * kMaxHeads);
+  const int qh0 = kvh * P.group + chunk * kMaxHeads;
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  if (tid == 0) s_st = read_state(P);
+  __syncthreads();
+  const tp_state st = s_st;
+  const int n_pages = min(max(st.n_pages, 0), P.page_capacity);
+  const int tail_len = min(max(st.tail_len, 0), kPage);
+  const int64_t tpos0 = (int64_t(st.first_page) + n_pages) * kPage;
+  const int valid = int(clamp64(int64_t(st.seq_len) - tpos0, 0, tail_len));
+  const int d = tid & (kD - 1), half = tid >> 7;
+  for (int h = 0; h < gc; ++h) {
+    float M = -INFINITY, L = 0.f, O = 0.f;
+    if (valid > 0) {
+      if (P.tail_f32) dense_tail_partial<float>(P, kvh, qh0 + h, valid, -1, s_sc, s_o, M, L, O);
+      else dense_tail_partial<__half>(P, kvh, qh0 + h, valid, -1, s_sc, s_o, M, L, O);
+    }
+    if (tid < kD) {
+      s_to[h * kD + tid] = O;
+      if (tid == 0) { s_tm[h][0] = M; s_tm[h][1] = L; }
+    }
+  }
+  // Record offsets (of the segment's first head), as split_combine_kernel computes them.
+  const Grid g = grid_of(P.num_kv_heads * P.nqc, n_pages, P.main_grid);
+  int n = 0;
+  if (P.owner) {
+    n = n_pages > 0 ? kConsumers : 0;
+    if (tid < n) soff[tid] = (vh * kConsumers + tid) * kPartialStride;
+  } else if (g.U > 0) {
+    const int c_lo = part_owner(g, vh * g.uph);
+    n = part_owner(g, vh * g.uph + g.uph - 1) - c_lo + 1;
+    for (int ci = tid; ci < n; ci += kCombineThreads) {
+      const int cc = c_lo + ci;
+      soff[ci] = (cc * 2 + (vh - part_begin(g, cc) / g.uph)) * kPartialStride;
+    }
+  }
+  __syncthreads();
+  float Mh[kMaxHeads], Lh[kMaxHeads], Oh[kMaxHeads];
+#pragma unroll
+  for (int h = 0; h < kMaxHeads; ++h) {
+    const bool own = h < gc && !half;
+    Mh[h] = own ? s_tm[h][0] : -INFINITY;
+    Lh[h] = own ? s_tm[h][1] : 0.f;
+    Oh[h] = own ? s_to[h * kD + d] : 0.f;
+  }
+  const int rc = kSegRecs / gc;  // records per chunk, all heads of each
+  const int rfl = gc * kRecFloats;
+  __syncthreads();  // the tail partials are in registers before the records overwrite them
+
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+#pragma unroll 1
+  for (int c0 = 0; c0 < n; c0 += rc) {
+    const int cn = min(rc, n - c0);
+    for (int i = tid; i < cn * (rfl / 4); i += kCombineThreads) {
+      const int ci = i / (rfl / 4), e = 4 * (i - ci * (rfl / 4));
+      cp_async16(&recs[ci * rfl + e], P.ws_partials + soff[c0 + ci] + e);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < kMaxHeads; ++h) {
+      if (h >= gc) continue;
+      const float* r = recs + h * kRecFloats;
+      float Mc = Mh[h];
+      for (int ci = half; ci < cn; ci += 2) Mc = fmaxf(Mc, r[ci * rfl]);
+      if (Mc != -INFINITY) {
+        const float a = (Mh[h] == -INFINITY) ? 0.f : exp2_approx(Mh[h] - Mc);
+        Lh[h] *= a;
+        Oh[h] *= a;
+        for (int ci = half; ci < cn; ci += 2) {
+          const float m = r[ci * rfl];
+          const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - Mc);
+          Lh[h] = fmaf(r[ci * rfl + 1], w, Lh[h]);
+          Oh[h] = fmaf(r[ci * rfl + 2 + d], w, Oh[h]);
+        }
+        Mh[h] = Mc;
+      }
+    }
+    __syncthreads();
+  }
+  // Halves: half 1 hands its (m, l, o) of every head to half 0 through the staging area.
+  if (half) {
+#pragma unroll
+    for (int h = 0; h < kMaxHeads; ++h) {
+      if (h >= gc) continue;
+      recs[(3 * h) * kD + d] = Mh[h];
+      recs[(3 * h + 1) * kD + d] = Lh[h];
+      recs[(3 * h + 2) * kD + d] = Oh[h];
+    }
+  }
+  __syncthreads();
+  if (!half) {
+#pragma unroll
+    for (int h = 0; h < kMaxHeads; ++h) {
+      if (h >= gc) continue;
+      const float m1 = recs[(3 * h) * kD + d], l1 = recs[(3 * h + 1) * kD + d], o1 = recs[(3 * h + 2) * kD + d];
+      const float Mx = fmaxf(Mh[h], m1);
+      float L = 0.f, O = 0.f;
+      if (Mx != -INFINITY) {
+        const float a0 = (Mh[h] == -INFINITY) ? 0.f : exp2_approx(Mh[h] - Mx);
+        const float a1 = (m1 == -INFINITY) ? 0.f : exp2_approx(m1 - Mx);
+        L = Lh[h] * a0 + l1 * a1;
+        O = Oh[h] * a0 + o1 * a1;
+      }
+      write_result(P, qh0 + h, d, Mx, L, O);
+    }
+  }
+}
+
 // ----------------------------------------------------------------------------- cross-shard combine
 __global__ void combine_kernel(const float* partials, int n_parts, int num_q_heads, __half* out) {
   const int h = blockIdx.x, d = threadIdx.x;
@@ -1660,6 +1794,9 @@ static cudaError_t reserve_smem(int variant, const void* page_pass, int smem) {
   if (e == cudaSuccess) e = cudaFuncSetAttribute(page_pass, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(reinterpret_cast<const void*>(split_combine_kernel),
+                             cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(segment_combine_kernel),
                              cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e == cudaSuccess) have = smem;
   return e;
@@ -2035,9 +2172,11 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
     const cudaError_t e = pass.launch(&mc, P);
     if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_decode_attention: ") + cudaGetErrorString(e));
   }
-  // Split combine as a programmatic dependent launch of the attention grid.
+  // Split combine as a programmatic dependent launch of the attention grid: one CTA per query
+  // head, or, for plain attention over more segments than SMs, one per segment.
+  const bool per_segment = !P.fused && P.xworld <= 1 && hkv * P.nqc > num_sms();
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(hkv * P.nqc * P.gmax);
+  cfg.gridDim = dim3(per_segment ? hkv * P.nqc : hkv * P.nqc * P.gmax);
   cfg.blockDim = dim3(kCombineThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
@@ -2046,7 +2185,7 @@ static int run_attention(const tp_page_pool* pool, const tp_tail* tail, tp_state
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, split_combine_kernel, P);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, per_segment ? segment_combine_kernel : split_combine_kernel, P);
   if (e != cudaSuccess) return fail(TP_ERR_CUDA, std::string("tp_decode_attention (combine): ") + cudaGetErrorString(e));
   return TP_OK;
 }
