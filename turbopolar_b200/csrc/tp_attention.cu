@@ -1575,11 +1575,14 @@ __global__ void __launch_bounds__(kCombineThreads, 5) split_combine_kernel(const
 // SMs, as a batch of sequences gives: one CTA per segment merges all gc query heads of the
 // segment, instead of one CTA per query head.  A workspace record holds the partials of every
 // head of its segment side by side, so one round of copies stages the records of all heads;
-// the heads' dense-tail partials run one after another before griddepcontrol.wait.  Per head
-// the arithmetic is split_combine_kernel's: the tail partial opens half 0, the records of even
-// and odd position merge in the two halves chunk by chunk (max, rescale, accumulate), and the
-// halves combine at the end.  A segment has at most 7 records here (whole-segment partition:
-// one per compute warp; whole waves: at most three CTAs), so one chunk holds them all.  Launched as a programmatic dependent of the
+// the heads' dense-tail partials run one after another before griddepcontrol.wait.  Per chunk
+// of records, thread h of the CTA takes head h's new maximum, the factor that rescales what
+// was merged before, the weight exp2(m - max) of every record and the new sum, once for all
+// 128 channels; each channel thread then rescales its accumulators and adds weight x o per
+// record (recomputing the weights in every channel thread, as split_combine_kernel does for
+// its one head, made this kernel instruction-bound at about 1,050 instructions a thread).  A
+// segment has at most 7 records here (whole-segment partition: one per compute warp; whole
+// waves: at most three CTAs), so one chunk holds them all.  Launched as a programmatic dependent of the
 // page pass like split_combine_kernel; its static shared memory is no larger, so a CTA fits
 // beside a page-pass CTA.
 constexpr int kSegRecs = 56;  // records of the staging area in one chunk (the rest: tail partials)
@@ -1632,76 +1635,71 @@ __global__ void __launch_bounds__(kCombineThreads, 4) segment_combine_kernel(con
     }
   }
   __syncthreads();
-  float Mh[kMaxHeads], Lh[kMaxHeads], Oh[kMaxHeads];
+  // Thread (half, d) owns channel d of heads half, half + 2, ...; the per-head running maximum,
+  // sum and rescale factor and the per-(record, head) weights are computed once, by thread h
+  // for head h, and read by every channel.
+  __shared__ float s_M[kMaxHeads], s_L[kMaxHeads], s_a[kMaxHeads], s_w[kSegRecs];
+  constexpr int kOwn = kMaxHeads / 2;
+  float Oh[kOwn];
 #pragma unroll
-  for (int h = 0; h < kMaxHeads; ++h) {
-    const bool own = h < gc && !half;
-    Mh[h] = own ? s_tm[h][0] : -INFINITY;
-    Lh[h] = own ? s_tm[h][1] : 0.f;
-    Oh[h] = own ? s_to[h * kD + d] : 0.f;
+  for (int j = 0; j < kOwn; ++j) {
+    const int h = half + 2 * j;
+    Oh[j] = h < gc ? s_to[h * kD + d] : 0.f;
+  }
+  if (tid < gc) {
+    s_M[tid] = s_tm[tid][0];
+    s_L[tid] = s_tm[tid][1];
   }
   const int rc = kSegRecs / gc;  // records per chunk, all heads of each
   const int rfl = gc * kRecFloats;
-  __syncthreads();  // the tail partials are in registers before the records overwrite them
+  const int q4 = rfl / 4;
+  __syncthreads();  // the tail partials are read before the records overwrite the staging area
 
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
 #pragma unroll 1
   for (int c0 = 0; c0 < n; c0 += rc) {
     const int cn = min(rc, n - c0);
-    for (int i = tid; i < cn * (rfl / 4); i += kCombineThreads) {
-      const int ci = i / (rfl / 4), e = 4 * (i - ci * (rfl / 4));
-      cp_async16(&recs[ci * rfl + e], P.ws_partials + soff[c0 + ci] + e);
+    for (int ci = 0; ci < cn; ++ci) {
+      const float* src = P.ws_partials + soff[c0 + ci];
+      for (int e = tid; e < q4; e += kCombineThreads) cp_async16(&recs[ci * rfl + 4 * e], src + 4 * e);
     }
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
-#pragma unroll
-    for (int h = 0; h < kMaxHeads; ++h) {
-      if (h >= gc) continue;
+    if (tid < gc) {
+      const int h = tid;
       const float* r = recs + h * kRecFloats;
-      float Mc = Mh[h];
-      for (int ci = half; ci < cn; ci += 2) Mc = fmaxf(Mc, r[ci * rfl]);
-      if (Mc != -INFINITY) {
-        const float a = (Mh[h] == -INFINITY) ? 0.f : exp2_approx(Mh[h] - Mc);
-        Lh[h] *= a;
-        Oh[h] *= a;
-        for (int ci = half; ci < cn; ci += 2) {
-          const float m = r[ci * rfl];
-          const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - Mc);
-          Lh[h] = fmaf(r[ci * rfl + 1], w, Lh[h]);
-          Oh[h] = fmaf(r[ci * rfl + 2 + d], w, Oh[h]);
-        }
-        Mh[h] = Mc;
+      const float M0 = s_M[h];
+      float Mc = M0;
+      for (int ci = 0; ci < cn; ++ci) Mc = fmaxf(Mc, r[ci * rfl]);
+      const float a = (M0 == -INFINITY) ? 0.f : exp2_approx(M0 - Mc);
+      float L = s_L[h] * a;
+      for (int ci = 0; ci < cn; ++ci) {
+        const float m = r[ci * rfl];
+        const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - Mc);
+        s_w[ci * gc + h] = w;
+        L = fmaf(r[ci * rfl + 1], w, L);
       }
+      s_a[h] = a;
+      s_M[h] = Mc;
+      s_L[h] = L;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kOwn; ++j) {
+      const int h = half + 2 * j;
+      if (h >= gc) continue;
+      const float* r = recs + h * kRecFloats + 2 + d;
+      float O = Oh[j] * s_a[h];
+      for (int ci = 0; ci < cn; ++ci) O = fmaf(r[ci * rfl], s_w[ci * gc + h], O);
+      Oh[j] = O;
     }
     __syncthreads();
   }
-  // Halves: half 1 hands its (m, l, o) of every head to half 0 through the staging area.
-  if (half) {
 #pragma unroll
-    for (int h = 0; h < kMaxHeads; ++h) {
-      if (h >= gc) continue;
-      recs[(3 * h) * kD + d] = Mh[h];
-      recs[(3 * h + 1) * kD + d] = Lh[h];
-      recs[(3 * h + 2) * kD + d] = Oh[h];
-    }
-  }
-  __syncthreads();
-  if (!half) {
-#pragma unroll
-    for (int h = 0; h < kMaxHeads; ++h) {
-      if (h >= gc) continue;
-      const float m1 = recs[(3 * h) * kD + d], l1 = recs[(3 * h + 1) * kD + d], o1 = recs[(3 * h + 2) * kD + d];
-      const float Mx = fmaxf(Mh[h], m1);
-      float L = 0.f, O = 0.f;
-      if (Mx != -INFINITY) {
-        const float a0 = (Mh[h] == -INFINITY) ? 0.f : exp2_approx(Mh[h] - Mx);
-        const float a1 = (m1 == -INFINITY) ? 0.f : exp2_approx(m1 - Mx);
-        L = Lh[h] * a0 + l1 * a1;
-        O = Oh[h] * a0 + o1 * a1;
-      }
-      write_result(P, qh0 + h, d, Mx, L, O);
-    }
+  for (int j = 0; j < kOwn; ++j) {
+    const int h = half + 2 * j;
+    if (h < gc) write_result(P, qh0 + h, d, s_M[h], s_L[h], Oh[j]);
   }
 }
 
