@@ -398,6 +398,25 @@ def test_large_batches_vs_oracle(batch, t, fmt):
         assert np.max(np.abs(step[b] - want)) < ATOL, b
 
 
+@pytest.mark.parametrize("batch,t", [(24, 100), (64, 150)])
+def test_large_batches_float32_tail_vs_oracle(batch, t):
+    """Float32 keys and values (so a float32 dense tail) over more segments than SMs: whole
+    waves of the flat partition (192 segments) and whole segments (512), with the records of
+    every segment merged for all its query heads in one CTA.  Every sequence matches the oracle."""
+    from turbopolar_b200 import TurboPolarKVCacheRuntime
+    cfg = _cfg(num_q_heads=32, num_kv_heads=8)
+    k, v = kv_inputs(250 + batch + t, 8 * batch, t, np.float32)
+    kb, vb = k.reshape(batch, 8, t, 128), v.reshape(batch, 8, t, 128)
+    q = np.random.default_rng(251 + batch + t).standard_normal((batch, 32, 128)).astype(np.float16)
+    rt = TurboPolarKVCacheRuntime(cfg, max_seq_len=t)
+    rt.append(T(kb), T(vb))
+    out = N(rt.attention(T(q))).astype(np.float64)
+    assert rt.read_device_error() == 0
+    for b in range(batch):
+        want = oracle_attention(q[b], kb[b:b + 1], vb[b:b + 1], fmt_of(cfg), cfg.use_int8_radii, cfg.attention_scale)
+        assert np.max(np.abs(out[b] - want)) < ATOL, b
+
+
 def test_full_size_c3_layer_vs_oracle():
     """One layer of config 3 at full size (32768 tokens, 32q/8kv) against the oracle."""
     from turbopolar_b200 import TurboPolarKVCacheRuntime
