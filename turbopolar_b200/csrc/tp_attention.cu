@@ -1511,10 +1511,18 @@ __global__ void __launch_bounds__(kCombineThreads, 5) split_combine_kernel(const
   __syncthreads();
 
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
-  // Two threads per channel: thread t merges the records of parity t >> 7 for channel t & 127;
-  // the halves are combined at the end (the dense-tail partial starts in half 0).
+  // Two threads per channel: thread t adds weight x o over the records of parity t >> 7 for
+  // channel t & 127 (the dense-tail partial starts in half 0).  Warp 0 takes each chunk's new
+  // maximum, the factor that rescales what was merged before, every record's weight
+  // exp2(m - max) and the new sum, once for all channels.
   const int d = tid & (kD - 1), half = tid >> 7;
-  float Mh = half ? -INFINITY : M, Lh = half ? 0.f : L, Oh = half ? 0.f : O;
+  __shared__ float s_w[kCombineChunk], s_run[3];  // weights; running max, sum, rescale factor
+  static_assert(kCombineChunk == 64, "warp 0 takes two records a lane");
+  float Oh = half ? 0.f : O;
+  if (tid == 0) {
+    s_run[0] = M;
+    s_run[1] = L;
+  }
 #pragma unroll 1
   for (int c0 = 0; c0 < n; c0 += kCombineChunk) {
     const int cn = min(kCombineChunk, n - c0);
@@ -1526,42 +1534,39 @@ __global__ void __launch_bounds__(kCombineThreads, 5) split_combine_kernel(const
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
-    float Mc = Mh;
-    for (int ci = half; ci < cn; ci += 2) Mc = fmaxf(Mc, sm.recs[ci][0]);
-    if (Mc != -INFINITY) {
-      const float a = (Mh == -INFINITY) ? 0.f : exp2_approx(Mh - Mc);
-      Lh *= a;
-      Oh *= a;
-#pragma unroll 4
-      for (int ci = half; ci < cn; ci += 2) {
-        const float m = sm.recs[ci][0];
-        const float w = (m == -INFINITY) ? 0.f : exp2_approx(m - Mc);
-        Lh = fmaf(sm.recs[ci][1], w, Lh);
-        Oh = fmaf(sm.recs[ci][2 + d], w, Oh);
+    if (tid < 32) {
+      const float M0 = s_run[0];
+      const bool has0 = tid < cn, has1 = tid + 32 < cn;
+      const float m0 = has0 ? sm.recs[tid][0] : -INFINITY, m1 = has1 ? sm.recs[tid + 32][0] : -INFINITY;
+      float Mc = fmaxf(M0, fmaxf(m0, m1));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) Mc = fmaxf(Mc, __shfl_xor_sync(0xffffffffu, Mc, o));
+      const float a = (M0 == -INFINITY) ? 0.f : exp2_approx(M0 - Mc);
+      const float w0 = (m0 == -INFINITY) ? 0.f : exp2_approx(m0 - Mc);
+      const float w1 = (m1 == -INFINITY) ? 0.f : exp2_approx(m1 - Mc);
+      if (has0) s_w[tid] = w0;
+      if (has1) s_w[tid + 32] = w1;
+      float l = (has0 ? sm.recs[tid][1] * w0 : 0.f) + (has1 ? sm.recs[tid + 32][1] * w1 : 0.f);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+      if (tid == 0) {
+        s_run[1] = fmaf(s_run[1], a, l);
+        s_run[0] = Mc;
+        s_run[2] = a;
       }
-      Mh = Mc;
     }
     __syncthreads();
+    Oh *= s_run[2];
+#pragma unroll 4
+    for (int ci = half; ci < cn; ci += 2) Oh = fmaf(sm.recs[ci][2 + d], s_w[ci], Oh);
+    __syncthreads();
   }
-  if (half) {
-    s_o[d] = Mh;
-    s_o[kD + d] = Lh;
-    s_o[2 * kD + d] = Oh;
-  }
+  if (half) s_o[d] = Oh;
   __syncthreads();
   if (!half) {
-    const float m1 = s_o[d], l1 = s_o[kD + d], o1 = s_o[2 * kD + d];
-    const float Mx = fmaxf(Mh, m1);
-    if (Mx != -INFINITY) {
-      const float a0 = (Mh == -INFINITY) ? 0.f : exp2_approx(Mh - Mx);
-      const float a1 = (m1 == -INFINITY) ? 0.f : exp2_approx(m1 - Mx);
-      L = Lh * a0 + l1 * a1;
-      O = Oh * a0 + o1 * a1;
-    } else {
-      L = 0.f;
-      O = 0.f;
-    }
-    M = Mx;
+    O = Oh + s_o[d];
+    M = s_run[0];
+    L = s_run[1];
   }
   __syncthreads();
   if (P.xworld > 1) {
