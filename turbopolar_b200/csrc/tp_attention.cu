@@ -720,8 +720,8 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity) { retu
 // no wait is ever more than one phase ahead of its barrier.  A thread dispatches one bulk copy
 // at a time, so the copies are spread over lanes that never hold up the warps that compute;
 // consumers get the same number of units to within one.
-// At most 192 registers a thread: 8 warps of the page pass and 8 of the split combine (64 each)
-// then fit the SM's 64K registers together (the CUDA-core comparison variant needs more).
+// At most 192 registers a thread: 8 warps of the page pass and 8 of a combine kernel (48 or 64
+// each) then fit the SM's 64K registers together (the CUDA-core comparison variant needs more).
 #if TP_QK_CUDA_CORES
 #define TP_PAGE_PASS_REGS 255
 #else
@@ -1402,7 +1402,8 @@ __device__ __forceinline__ void advance_state(const AttnParams& P, const tp_stat
   P.d_state[5] = 0;
 }
 
-// At most 64 registers a thread, so a split-combine CTA fits beside a page-pass CTA (177).
+// At most 48 registers a thread (five CTAs on an SM once the page pass has finished; one fits
+// beside a page-pass CTA of up to 192 registers).
 __global__ void __launch_bounds__(kCombineThreads, 5) split_combine_kernel(const __grid_constant__ AttnParams P) {
   __shared__ __align__(16) CombineSmem sm;
   __shared__ int soff[kMaxContrib];
