@@ -113,3 +113,30 @@ def test_whole_segment_unit_order_and_records():
                 assert segs == sorted(segs)  # one run per segment
                 seen.update(units)
             assert seen == {(sl, j) for sl in range(nseg) for j in range(uph)}
+
+
+SEG_RECS = 56  # kSegRecs: records of all heads that segment_combine_kernel stages in one chunk
+MAX_HEADS = 8  # kMaxHeads: query heads of one segment
+
+
+def test_segment_combine_records_fit_one_chunk():
+    """segment_combine_kernel (plain attention over more segments than SMs) stages the records
+    of every head of a segment at once: seven per segment with whole segments (one per compute
+    warp), at most three with whole waves; times at most eight heads, within its 56 records."""
+    for segs in list(range(149, 3000, 11)) + [152, 192, 200, 296, 320, 512, 1024]:
+        grid, owner = grid_size(segs)
+        if owner:
+            n_max = CONSUMERS
+        else:
+            n_max = 0
+            for n_pages in (1, 2, 3, 64):
+                uph = 2 * n_pages
+                U = segs * uph
+                C = min(U, grid)
+                begin = [part_begin(c, U, C) for c in range(C + 1)]
+                per_seg = [0] * segs
+                for c in range(C):
+                    for s_ in range(begin[c] // uph, (begin[c + 1] - 1) // uph + 1):
+                        per_seg[s_] += 1
+                n_max = max(n_max, max(per_seg))
+        assert n_max * MAX_HEADS <= SEG_RECS, (segs, n_max)
